@@ -1,0 +1,46 @@
+#pragma once
+// Owner of physical KV page ids and their reference counts (reference:
+// include/kvflux/physical_block_pool.h:11-58). Pure metadata: it allocates no
+// device memory. PagedKVStorage turns an id into a device address.
+#include "kvflux/block_manager.h"
+
+#include <cstddef>
+
+namespace kvflux {
+
+// Index of a physical page in the KV cache; not a pointer, not ownership.
+using PhysicalBlockID = std::size_t;
+using PhysicalBlockHandle = BlockHandle;
+
+// Single-threaded, like BlockManager; callers lock across threads.
+class PhysicalBlockPool {
+public:
+    PhysicalBlockPool(std::size_t capacity, std::size_t block_size,
+                      BlockManager::Hasher hasher = BlockManager::prefix_hash);
+
+    PhysicalBlockPool(const PhysicalBlockPool&) = delete;
+    PhysicalBlockPool& operator=(const PhysicalBlockPool&) = delete;
+    PhysicalBlockPool(PhysicalBlockPool&&) = delete;
+    PhysicalBlockPool& operator=(PhysicalBlockPool&&) = delete;
+
+    PhysicalBlockHandle allocate();
+    void retain(PhysicalBlockHandle handle);
+    void free(PhysicalBlockHandle handle);
+
+    void publish(PhysicalBlockHandle handle, const Tokens& prefix);
+    bool lookup(const Tokens& prefix, PhysicalBlockHandle& out);
+    bool is_published(PhysicalBlockHandle handle) const;
+
+    // Only a live handle yields an id; a stale generation throws invalid_argument.
+    PhysicalBlockID id(PhysicalBlockHandle handle) const;
+    std::size_t ref_count(PhysicalBlockHandle handle) const;
+    std::size_t capacity() const noexcept;
+    std::size_t block_size() const noexcept;
+    // Pages that can be handed out now: free plus evictable idle cached pages.
+    std::size_t available() const noexcept;
+
+private:
+    BlockManager manager_;
+};
+
+} // namespace kvflux

@@ -1,0 +1,155 @@
+/*
+ * kvfx.h - C ABI of the B200 (sm_100a) paged-KV data path.
+ *
+ * Plain pointers and sizes only: no C++ or torch types cross this boundary, so
+ * any FFI (ctypes, cgo, JNI, N-API) can bind it. Every entry point is
+ * stream-ordered: it enqueues work on `stream` (a cudaStream_t; NULL is the
+ * legacy default stream) and returns without synchronising. Device arrays
+ * must be resident on `cache->device`. Return value: KVFX_OK or an error code;
+ * kvfx_last_error() gives a message for the calling thread's last failure.
+ *
+ * The cache layout is the reference's single-layer paged layout
+ * (src/v2/paged_kv_layout.cpp:27-68 in KVFlux):
+ *     K[num_blocks][num_kv_heads][block_size][head_size], then V alike,
+ * and a slot id is physical_block * block_size + offset_in_block
+ * (src/v2/slot_mapping.cpp:29).
+ *
+ * These entry points trust the tables they are given only as far as memory
+ * safety: a slot or block id at or beyond the cache is skipped (writes) or
+ * read as nothing, and sets KVFX_FLAG_BAD_INDEX in the device status word
+ * (kvfx_device_status). The C++ API in include/kvflux/v2 validates everything
+ * on the host first and raises the reference's exception types.
+ */
+#ifndef KVFX_H
+#define KVFX_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes. */
+#define KVFX_OK 0
+#define KVFX_EINVAL 1       /* bad argument: null pointer, bad shape or dtype   */
+#define KVFX_ERANGE 2       /* index outside the cache                           */
+#define KVFX_EOVERFLOW 3    /* size arithmetic overflow                          */
+#define KVFX_ECUDA 4        /* CUDA runtime error (message in kvfx_last_error)   */
+#define KVFX_ETIMEOUT 5     /* a bounded device-side wait gave up                */
+#define KVFX_ENOSPACE 6     /* workspace smaller than the *_workspace_bytes size */
+
+/* Cache element types (same order as kvflux::DType). */
+#define KVFX_F16 0
+#define KVFX_BF16 1
+#define KVFX_F32 2
+
+/* Bits of the per-device status word. */
+#define KVFX_FLAG_BAD_INDEX 1u  /* a slot/block id beyond the cache was skipped */
+#define KVFX_FLAG_TIMEOUT 2u    /* a bounded wait inside a kernel expired        */
+
+typedef struct kvfx_cache {
+    void* k_base;            /* device address of K[0][0][0][0]                  */
+    void* v_base;            /* device address of V[0][0][0][0]                  */
+    uint64_t num_blocks;     /* physical pages                                   */
+    uint32_t num_kv_heads;
+    uint32_t block_size;     /* tokens per page                                  */
+    uint32_t head_size;
+    uint32_t dtype;          /* KVFX_F16 / KVFX_BF16 / KVFX_F32                  */
+    int32_t device;          /* CUDA ordinal holding the cache                   */
+    uint32_t reserved;       /* must be 0                                        */
+} kvfx_cache;
+
+/*
+ * Paged KV write: for token i, K[slot_i / bs][h][slot_i % bs][:] = k_new[i][h][:]
+ * and the same for V, for all h. k_new/v_new: [num_tokens][num_kv_heads][head_size]
+ * in the cache dtype; slots: device uint64[num_tokens], pairwise distinct.
+ * Replaces the kernel launch of write_paged_kv (KVFlux src/v2/paged_kv_write.cu:86-97).
+ */
+int kvfx_write(const kvfx_cache* cache, const void* k_new, const void* v_new,
+               const uint64_t* slots, uint64_t num_tokens, void* stream);
+
+/*
+ * Gather of one sequence: k_out[t][h][:] = K[blocks[t / bs]][h][t % bs][:] for
+ * t < num_tokens (V alike). blocks: device uint64[ceil(num_tokens / bs)].
+ * Outputs must not overlap each other or the cache.
+ * Replaces the kernel launch of read_paged_kv (KVFlux src/v2/paged_kv_read.cu:90-102).
+ */
+int kvfx_gather(const kvfx_cache* cache, const uint64_t* blocks, uint64_t num_tokens,
+                void* k_out, void* v_out, void* stream);
+
+/*
+ * Batched gather: sequence b has seq_lens[b] tokens, pages in row b of the
+ * row-major table blocks[batch][max_blocks_per_seq], and outputs k_out[b] /
+ * v_out[b] (device arrays of device pointers). One launch for the whole batch.
+ * No counterpart in the reference, which gathers one sequence per call.
+ */
+int kvfx_gather_batch(const kvfx_cache* cache, const uint64_t* blocks,
+                      const uint64_t* seq_lens, uint64_t batch, uint64_t max_blocks_per_seq,
+                      void* const* k_out, void* const* v_out, void* stream);
+
+/*
+ * Whole-page copy of K and V from src_block to dst_block (byte-exact).
+ * Replaces the two cudaMemcpyAsync of PagedKVStorage::copy_block
+ * (KVFlux src/v2/paged_kv_storage.cpp:70-93).
+ */
+int kvfx_copy_page(const kvfx_cache* cache, uint64_t src_block, uint64_t dst_block,
+                   void* stream);
+
+/*
+ * Batch decode PagedAttention: one last-position query per sequence.
+ *   q, o         : device float[batch][q_heads][head_size]
+ *   block_table  : device uint64[batch][max_blocks_per_seq], row b holds the
+ *                  pages of sequence b (entries past its length are not read)
+ *   seq_lens     : device uint64[batch], each in [1, max_seq_len]
+ *   max_seq_len  : host-side upper bound of seq_lens (sizes the grid)
+ *   pages_per_split: split-K chunk in pages; 0 chooses one from the shape
+ *   workspace    : device scratch of kvfx_decode_workspace_bytes(...) bytes,
+ *                  zero-filled before its first use and left reusable
+ *                  (the kernels reset what they use).
+ * q_heads must be a multiple of num_kv_heads; Q head j uses KV head
+ * j / (q_heads / num_kv_heads). Scale 1/sqrt(head_size).
+ * Replaces paged_attention_batch's launch (KVFlux src/v2/paged_attention.cu:248-313).
+ */
+uint64_t kvfx_decode_workspace_bytes(const kvfx_cache* cache, uint64_t batch,
+                                     uint32_t q_heads, uint64_t max_seq_len,
+                                     uint32_t pages_per_split);
+uint32_t kvfx_decode_pages_per_split(const kvfx_cache* cache, uint64_t batch,
+                                     uint32_t q_heads, uint64_t max_seq_len,
+                                     uint64_t total_tokens);
+int kvfx_decode(const kvfx_cache* cache, const float* q, float* o,
+                const uint64_t* block_table, const uint64_t* seq_lens, uint64_t batch,
+                uint64_t max_blocks_per_seq, uint32_t q_heads, uint64_t max_seq_len,
+                uint32_t pages_per_split, void* workspace, uint64_t workspace_bytes,
+                void* stream);
+
+/*
+ * Single-sequence causal PagedAttention with query_tokens queries aligned to
+ * the end of the kv_tokens-long sequence (query i sees positions
+ * <= kv_tokens - query_tokens + i). q, o: device float[query_tokens][q_heads][head_size];
+ * blocks: device uint64[ceil(kv_tokens / bs)].
+ * Replaces paged_attention's launch (KVFlux src/v2/paged_attention.cu:193-246).
+ */
+uint64_t kvfx_attention_workspace_bytes(const kvfx_cache* cache, uint64_t query_tokens,
+                                        uint64_t kv_tokens, uint32_t q_heads);
+int kvfx_attention(const kvfx_cache* cache, const float* q, float* o, const uint64_t* blocks,
+                   uint64_t query_tokens, uint64_t kv_tokens, uint32_t q_heads,
+                   void* workspace, uint64_t workspace_bytes, void* stream);
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char* kvfx_last_error(void);
+
+/*
+ * Reads the status word of `device` (KVFX_FLAG_* bits set by kernels since
+ * the last clear) after the caller has synchronised the work in question;
+ * clears it when `clear` is non-zero.
+ */
+int kvfx_device_status(int device, uint32_t* flags, int clear);
+
+/* Library version, e.g. "kvflux-b200 0.1.0 sm_100a". */
+const char* kvfx_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVFX_H */

@@ -1,0 +1,74 @@
+// Internal helpers of the C++ data plane: the per-storage runtime (reusable
+// device/pinned scratch, decode workspace, duplicate-slot bitmap), the device
+// guard, pointer validation, and the mapping of C-ABI codes to the
+// reference's exception types.
+#pragma once
+
+#include <cuda_runtime_api.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "kvflux/v2/paged_kv_storage.h"
+#include "kvfx.h"
+
+namespace kvflux::v2::detail {
+
+[[noreturn]] void throw_cuda(const char* op, cudaError_t e);
+inline void cuda_check(cudaError_t e, const char* op) {
+    if (e != cudaSuccess) throw_cuda(op, e);
+}
+
+// Throws the exception type the reference raises for this C-ABI code.
+void check_kvfx(int code, const char* op);
+
+std::size_t mul_checked(std::size_t a, std::size_t b, const char* what);
+
+// Switches to `device` for a scope and restores the previous device.
+class DeviceGuard {
+public:
+    explicit DeviceGuard(int device);
+    ~DeviceGuard() noexcept;
+    DeviceGuard(const DeviceGuard&) = delete;
+    DeviceGuard& operator=(const DeviceGuard&) = delete;
+
+private:
+    int previous_ = 0;
+};
+
+// invalid_argument unless `p` is device memory (cudaMemoryTypeDevice) of `device`.
+void require_device_pointer(const void* p, int device, const char* name);
+bool overlaps(const void* a, std::size_t a_bytes, const void* b, std::size_t b_bytes);
+
+struct StorageRuntime {
+    kvfx_cache cache{};
+    int device = 0;
+
+    // Device scratch for per-call tables and the pinned host staging that
+    // feeds it; both grow and are reused, never shrink.
+    void* dev_scratch = nullptr;
+    std::size_t dev_bytes = 0;
+    void* pinned = nullptr;
+    std::size_t pinned_bytes = 0;
+
+    // Decode/attention workspace, zero-filled when (re)allocated; the kernels
+    // leave it reusable.
+    void* workspace = nullptr;
+    std::size_t workspace_bytes = 0;
+
+    // One bit per slot for the duplicate check of write_paged_kv.
+    std::vector<std::uint64_t> seen;
+
+    ~StorageRuntime();
+    // Copies `n` arrays (host pointers and byte counts) into device scratch
+    // with one H2D copy on the legacy default stream; returns device pointers.
+    void upload(const void* const* host, const std::size_t* bytes, int n, void** device_out);
+    void* ensure_workspace(std::size_t bytes);
+    // Synchronises the legacy default stream and raises on device-side flags.
+    void finish(const char* op) const;
+};
+
+} // namespace kvflux::v2::detail

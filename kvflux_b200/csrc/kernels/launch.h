@@ -1,0 +1,111 @@
+// Host-side declarations of the kernel launchers (internal to the library).
+// Every launcher enqueues on `stream` and returns the launch's cudaError_t.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kvfx.h"
+
+namespace kvfx {
+
+__host__ __device__ constexpr uint64_t ceil_div(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
+__host__ __device__ constexpr uint64_t umin64(uint64_t a, uint64_t b) { return a < b ? a : b; }
+
+// Validated, derived view of a kvfx_cache.
+struct CacheView {
+    char* k;
+    char* v;
+    uint64_t num_blocks;
+    uint32_t heads, bs, hd, dtype, elem;
+    uint64_t row_bytes;        // head_size * elem: one (token, head) row
+    uint64_t chunk_bytes;      // block_size * row_bytes: one head of one page
+    uint64_t page_bytes;       // heads * chunk_bytes
+    uint64_t slot_count;       // num_blocks * block_size
+    int device;
+};
+
+// Largest vector width in {16, 8, 4, 2, 1} bytes dividing `bytes` and every
+// address in `ptrs` (n of them).
+uint32_t vector_width(uint64_t bytes, const void* const* ptrs, int n);
+
+cudaError_t launch_write(const CacheView& c, const void* k_new, const void* v_new,
+                         const uint64_t* slots, uint64_t n, unsigned* status, cudaStream_t s);
+
+cudaError_t launch_copy_page(const CacheView& c, uint64_t src, uint64_t dst, unsigned* status,
+                             cudaStream_t s);
+
+// Gather of `batch` sequences. If `per_seq_out` is false, k_out/v_out point to
+// a single sequence's outputs (batch must be 1) and `single_blocks`/`single_len`
+// describe it; otherwise k_out/v_out are device arrays of device pointers and
+// the block table is row-major [batch][max_blocks].
+struct GatherArgs {
+    const uint64_t* blocks;    // [batch][max_blocks] (batch == 1: the one row)
+    const uint64_t* lens;      // device lengths, or nullptr when batch == 1
+    uint64_t single_len;       // length when lens == nullptr
+    uint64_t batch, max_blocks;
+    void* const* k_out_list;   // device array (batched) or nullptr
+    void* const* v_out_list;
+    void* k_out;               // single-sequence outputs
+    void* v_out;
+    uint64_t max_len;          // host bound of the lengths (grid sizing)
+};
+cudaError_t launch_gather(const CacheView& c, const GatherArgs& a, unsigned* status, cudaStream_t s);
+
+struct DecodeArgs {
+    const float* q;
+    float* o;
+    const uint64_t* table;
+    const uint64_t* lens;
+    uint64_t batch, max_blocks, max_len;
+    uint32_t q_heads, pages_per_split;
+    void* workspace;
+    uint64_t workspace_bytes;
+};
+uint64_t decode_workspace_bytes(const CacheView& c, uint64_t batch, uint32_t q_heads,
+                                uint64_t max_len, uint32_t pages_per_split);
+uint32_t decode_pages_per_split(const CacheView& c, uint64_t batch, uint32_t q_heads,
+                                uint64_t max_len, uint64_t total_tokens);
+cudaError_t launch_decode(const CacheView& c, const DecodeArgs& a, unsigned* status, cudaStream_t s);
+
+struct AttentionArgs {
+    const float* q;
+    float* o;
+    const uint64_t* blocks;
+    uint64_t query_tokens, kv_tokens;
+    uint32_t q_heads;
+    void* workspace;
+    uint64_t workspace_bytes;
+};
+uint64_t attention_workspace_bytes(const CacheView& c, uint64_t query_tokens, uint64_t kv_tokens,
+                                   uint32_t q_heads);
+cudaError_t launch_attention(const CacheView& c, const AttentionArgs& a, unsigned* status,
+                             cudaStream_t s);
+
+// Generic SIMT attention over "query rows" (used by both entry points for the
+// shapes the specialised kernels do not cover).
+struct GenericAttnArgs {
+    const float* q;
+    float* o;
+    const uint64_t* blocks;     // row-major table, row stride `row_stride`
+    uint64_t row_stride;        // 0: every query row uses row 0 (single sequence)
+    const uint64_t* lens;       // batch mode: device lengths, one query per sequence
+    uint64_t units;             // batch size, or query_tokens for a single sequence
+    uint64_t kv_tokens;         // single-sequence mode: sequence length
+    uint32_t q_heads;
+};
+cudaError_t launch_attention_generic(const CacheView& c, const GenericAttnArgs& a,
+                                     unsigned* status, cudaStream_t s);
+
+// Tensor maps over the K and V caches for the TMA-fed kernels (cached per cache).
+struct CacheMaps {
+    CUtensorMap k;
+    CUtensorMap v;
+    bool valid;
+};
+const CacheMaps* cache_maps(const CacheView& c, cudaError_t* err);
+
+int device_sm_count(int device);
+
+}  // namespace kvfx
