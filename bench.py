@@ -1,0 +1,654 @@
+"""Benchmark of the B200 paged-KV data path.
+
+Headline: batch-decode PagedAttention KV GB/s on the Llama-3-70B head shape
+(config 5: 64 Q / 8 KV heads, head_size 128, bf16 KV, FP32 Q/O, batch 256,
+sequence lengths uniform in [4096, 32768], block 16, randomly fragmented
+pools). With N GPUs the KV heads are sharded: rank g owns KV heads
+[g*8/N, (g+1)*8/N) and their Q heads, with its own pool and block tables; the
+timed region has no collective. `value` = KV bytes of all ranks / max-over-
+ranks time per step (strong scaling: the job is fixed, N splits it).
+
+The same JSON line carries: `e2e` (the same metric through the drop-in C++
+API paged_attention_batch with Q on pinned host memory, H2D + D2H inside the
+timed region), `roofline` of the decode kernel, `cpu_baseline` (the
+reference's CPU path on a bounded sample, rank 0 at N=1), clocks, and
+`secondary` lines: KV-write tokens/s and gather GB/s on config 2 (64
+sequences x 8192 tokens, 256 new tokens per step, odd/even fragmented
+65,536-page pool) and decode GB/s on config 3 (Llama-3-8B heads, batch 64,
+lengths in [512, 8192]).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Inputs are synthetic (seeded). Decode and gather inputs are far larger than
+the 126 MB L2, so no flush is needed between timed steps; the 2 MB write
+step is reported per launch and over graph-captured back-to-back launches.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode paged-attn KV GB/s (% HBM peak) + KV-write tokens/s at 1/2/4/8 B200"
+HBM_FALLBACK_GBS = 6650.0
+DATASHEET_GBS = 7700.0
+
+
+def load_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return HBM_FALLBACK_GBS, "fallback"
+
+
+def traffic_ratio(kernel: str):
+    """DRAM bytes per algorithmic byte from a committed ncu summary, if any."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if not p.exists():
+        return None, None
+    d = json.loads(p.read_text()).get(kernel)
+    if not d:
+        return None, None
+    return float(d["dram_bytes_per_algorithmic_byte"]), d.get("capture")
+
+
+# ------------------------------------------------------------------ ranks ---
+
+class Ranks:
+    def __init__(self, gpus: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.world > 1 and self.world != gpus:
+            raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={self.world}")
+        self.dist = None
+
+    def init_gpu(self):
+        import datetime
+
+        import torch
+
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                                    device_id=torch.device("cuda", self.local))
+            self.dist = dist
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+
+    def reduce(self, x: float, op: str) -> float:
+        if self.dist is None:
+            return x
+        import torch
+
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX if op == "max" else self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.dist is not None:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------- clocks ---
+
+class Clocks:
+    """Samples nvidia-smi clocks and throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device, self.proc, self.path = device, None, None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=fd, stderr=subprocess.DEVNULL)
+            os.close(fd)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], [], set()
+        for line in Path(self.path).read_text().splitlines():
+            r = [x.strip() for x in line.split(",")]
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for name, val in zip(self.NAMES, r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------- raw memory ---
+
+_RT = None
+
+
+def cudart():
+    global _RT
+    if _RT is None:
+        import torch
+
+        torch.cuda.init()
+        _RT = ctypes.CDLL("libcudart.so.12")
+        _RT.cudaMemcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
+    return _RT
+
+
+def d2h(addr: int, out: np.ndarray) -> None:
+    assert cudart().cudaMemcpy(out.ctypes.data, addr, out.nbytes, 2) == 0
+
+
+# ------------------------------------------------------------ workloads ---
+
+def fill_cache(kv, storage, seqs, seed: int, chunk_tokens: int = 1 << 16):
+    """Writes N(0,1) bf16 K/V into every reserved slot through kvfx_write."""
+    import torch
+
+    desc = kv.cache_descriptor(storage)
+    lay = storage.layout()
+    heads, hd, bs = lay.num_kv_heads(), lay.head_size(), lay.block_size()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    parts = []
+    for s in seqs:
+        n = s.num_tokens()
+        tbl = np.array(kv.build_read_block_table(s), np.uint64)
+        t = np.arange(n, dtype=np.uint64)
+        parts.append(tbl[t // bs] * bs + t % bs)
+    slots = np.concatenate(parts)
+    kbuf = torch.empty(chunk_tokens * heads * hd, dtype=torch.bfloat16, device="cuda")
+    vbuf = torch.empty_like(kbuf)
+    for start in range(0, len(slots), chunk_tokens):
+        part = slots[start:start + chunk_tokens]
+        n = len(part)
+        kbuf[: n * heads * hd].normal_(generator=gen)
+        vbuf[: n * heads * hd].normal_(generator=gen)
+        sd = torch.from_numpy(part.view(np.int64)).cuda()
+        kv.check(kv.lib.kvfx_write(ctypes.byref(desc), kbuf.data_ptr(), vbuf.data_ptr(), sd.data_ptr(), n, None),
+                 "fill kvfx_write")
+    torch.cuda.synchronize()
+
+
+class Decode:
+    """One rank's shard of a batch-decode config."""
+
+    def __init__(self, kv, w, cfg: dict, rank: int, world: int):
+        import torch
+
+        self.kv, self.cfg = kv, cfg
+        assert cfg["kv_heads"] % world == 0
+        self.kvh = cfg["kv_heads"] // world
+        self.qh = cfg["q_heads"] // world
+        self.hd, self.bs = cfg["head_size"], cfg["block_size"]
+        self.lens = w.config_lengths(cfg).astype(np.uint64)
+        self.batch = len(self.lens)
+        pages = int(sum((int(l) + self.bs - 1) // self.bs for l in self.lens))
+        cap = cfg.get("pool_pages") or (1 << int(math.ceil(math.log2(pages * 1.25))))
+        self.b = w.decode_batch_on_pool(cap, self.bs, self.lens, seed=cfg["seed"] * 131 + rank, mode="random")
+        dev = torch.cuda.current_device()
+        self.storage = kv.PagedKVStorage(self.b.pool, self.kvh, self.hd, kv.DType.BFloat16, dev)
+        fill_cache(kv, self.storage, self.b.sequences, seed=cfg["seed"] * 7 + rank)
+        self.table_np, self.width = self.b.table()
+        self.table = torch.from_numpy(self.table_np.view(np.int64)).cuda()
+        self.lens_d = torch.from_numpy(self.lens.view(np.int64)).cuda()
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(cfg["seed"] * 3 + rank)
+        self.q = torch.randn(self.batch * self.qh * self.hd, generator=gen, device="cuda", dtype=torch.float32)
+        self.o = torch.empty_like(self.q)
+        self.desc = kv.cache_descriptor(self.storage)
+        self.max_len = int(self.lens.max())
+        self.pps = kv.lib.kvfx_decode_pages_per_split(ctypes.byref(self.desc), self.batch, self.qh, self.max_len,
+                                                      int(self.lens.sum()))
+        ws = kv.lib.kvfx_decode_workspace_bytes(ctypes.byref(self.desc), self.batch, self.qh, self.max_len, self.pps)
+        self.ws = torch.zeros(max(int(ws), 16), dtype=torch.uint8, device="cuda")
+        self.kv_bytes = int(self.lens.sum()) * self.kvh * self.hd * 2 * 2
+        self.alg_bytes = self.kv_bytes + 2 * self.q.numel() * 4 + self.batch * (self.width + 1) * 8
+
+    def launch(self, stream: int | None) -> None:
+        rc = self.kv.lib.kvfx_decode(ctypes.byref(self.desc), self.q.data_ptr(), self.o.data_ptr(),
+                                     self.table.data_ptr(), self.lens_d.data_ptr(), self.batch, self.width, self.qh,
+                                     self.max_len, self.pps, self.ws.data_ptr(), self.ws.numel(), stream)
+        self.kv.check(rc, "kvfx_decode")
+
+    def host_sample(self, requests):
+        """Pages of `requests` copied to a compact host cache (for the CPU leg)."""
+        page_bytes = self.storage.layout().page_bytes()
+        ids = [self.table_np[r, :(int(self.lens[r]) + self.bs - 1) // self.bs] for r in requests]
+        uniq = np.unique(np.concatenate(ids))
+        remap = {int(p): i for i, p in enumerate(uniq)}
+        hk = np.empty((len(uniq), page_bytes), np.uint8)
+        hv = np.empty_like(hk)
+        for i, p in enumerate(uniq):
+            d2h(self.storage.key_base() + int(p) * page_bytes, hk[i])
+            d2h(self.storage.value_base() + int(p) * page_bytes, hv[i])
+        width = max(len(x) for x in ids)
+        table = np.zeros((len(requests), width), np.uint64)
+        for j, x in enumerate(ids):
+            table[j, :len(x)] = [remap[int(p)] for p in x]
+        q = self.q.view(self.batch, -1)[list(requests)].cpu().numpy().reshape(-1)
+        o = self.o.view(self.batch, -1)[list(requests)].cpu().numpy().reshape(-1)
+        return hk.reshape(-1), hv.reshape(-1), len(uniq), table, self.lens[list(requests)].copy(), q, o
+
+
+def time_launches(launch, steps: int, warmup: int, ranks: Ranks):
+    """Device time of each of `steps` launches (CUDA events on the launching
+    stream), after `warmup` untimed ones; barrier + synchronize on both sides."""
+    import torch
+
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            launch(sp)
+    torch.cuda.synchronize()
+    ranks.barrier()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    with torch.cuda.stream(stream):
+        ev[0].record(stream)
+        for i in range(steps):
+            launch(sp)
+            ev[i + 1].record(stream)
+    torch.cuda.synchronize()
+    ranks.barrier()
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
+    return per, ev[0].elapsed_time(ev[steps])
+
+
+def e2e_decode(kv, wl: Decode, steps: int, warmup: int):
+    """Same metric through paged_attention_batch: Q from pinned host memory
+    (H2D), the API call (which uploads the block table and lengths from the
+    host, launches and synchronises), and O back to pinned host memory."""
+    import torch
+
+    q_host = wl.q.cpu().pin_memory()
+    o_host = torch.empty_like(q_host).pin_memory()
+    seqs = wl.b.sequences
+    table_bytes = wl.batch * wl.width * 8 + wl.batch * 8
+
+    def step():
+        wl.q.copy_(q_host, non_blocking=True)
+        kv.paged_attention_batch(wl.storage, seqs, wl.q, wl.o, wl.qh)
+        o_host.copy_(wl.o, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    wall = time.perf_counter()
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall
+    ms = max(t0.elapsed_time(t1), wall * 1e3) / steps
+    return ms, q_host.numel() * 4 + table_bytes, o_host.numel() * 4
+
+
+class WriteGather:
+    """Config 2 on one rank's KV-head shard."""
+
+    def __init__(self, kv, w, cfg: dict, rank: int, world: int):
+        import torch
+
+        self.kv = kv
+        self.heads = cfg["kv_heads"] // world
+        self.hd, self.bs = cfg["head_size"], cfg["block_size"]
+        nseq, pre, new = cfg["sequences"], cfg["prefill"], cfg["new_tokens"]
+        self.total_len = pre + new
+        lens = [self.total_len] * nseq
+        b = w.decode_batch_on_pool(cfg["pool_pages"], self.bs, lens, seed=cfg["seed"] + rank, mode="odd")
+        self.b = b
+        dev = torch.cuda.current_device()
+        self.storage = kv.PagedKVStorage(b.pool, self.heads, self.hd, kv.DType.BFloat16, dev)
+        fill_cache(kv, self.storage, b.sequences, seed=cfg["seed"] * 5 + rank)
+        self.desc = kv.cache_descriptor(self.storage)
+        # The step's 256 slots: the last `new` positions of every sequence.
+        self.slots_np = np.array(kv.build_slot_mapping([(s, p) for s in b.sequences
+                                                        for p in range(pre, pre + new)]), np.uint64)
+        self.n = len(self.slots_np)
+        self.slots = torch.from_numpy(self.slots_np.view(np.int64)).cuda()
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(cfg["seed"] + 17 * rank)
+        self.k_new = torch.randn(self.n * self.heads * self.hd, generator=gen, device="cuda").to(torch.bfloat16)
+        self.v_new = torch.randn_like(self.k_new, dtype=torch.float32).to(torch.bfloat16)
+        table, self.width = b.table()
+        self.table = torch.from_numpy(table.view(np.int64)).cuda()
+        self.lens = torch.full((nseq,), self.total_len, dtype=torch.int64, device="cuda")
+        self.nseq = nseq
+        per = self.total_len * self.heads * self.hd
+        self.k_out = torch.empty(nseq * per, dtype=torch.bfloat16, device="cuda")
+        self.v_out = torch.empty_like(self.k_out)
+        ptrs_k = np.array([self.k_out.data_ptr() + i * per * 2 for i in range(nseq)], np.uint64)
+        ptrs_v = np.array([self.v_out.data_ptr() + i * per * 2 for i in range(nseq)], np.uint64)
+        self.pk = torch.from_numpy(ptrs_k.view(np.int64)).cuda()
+        self.pv = torch.from_numpy(ptrs_v.view(np.int64)).cuda()
+        self.write_bytes = self.n * self.heads * self.hd * 2 * 2 * 2 + self.n * 8  # read+write K,V + slots
+        self.gather_bytes = 2 * 2 * nseq * per * 2 + table.nbytes  # read+write K,V + table
+
+    def write(self, stream):
+        self.kv.check(self.kv.lib.kvfx_write(ctypes.byref(self.desc), self.k_new.data_ptr(), self.v_new.data_ptr(),
+                                             self.slots.data_ptr(), self.n, stream), "kvfx_write")
+
+    def gather(self, stream):
+        self.kv.check(self.kv.lib.kvfx_gather_batch(ctypes.byref(self.desc), self.table.data_ptr(),
+                                                    self.lens.data_ptr(), self.nseq, self.width, self.pk.data_ptr(),
+                                                    self.pv.data_ptr(), stream), "kvfx_gather_batch")
+
+    def graph_write_ms(self, launches: int = 100) -> float:
+        """Per-launch time of `launches` back-to-back writes captured in a CUDA graph."""
+        import torch
+
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            self.write(s.cuda_stream)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(launches):
+                self.write(s.cuda_stream)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) / (reps * launches)
+
+    def e2e_write_ms(self, steps: int = 20) -> tuple[float, int]:
+        import torch
+
+        kh = self.k_new.cpu().pin_memory()
+        vh = self.v_new.cpu().pin_memory()
+        slots = [int(x) for x in self.slots_np]
+
+        def step():
+            self.k_new.copy_(kh, non_blocking=True)
+            self.v_new.copy_(vh, non_blocking=True)
+            self.kv.write_paged_kv(self.storage, self.k_new, self.v_new, slots)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        for _ in range(steps):
+            step()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t) * 1e3 / steps, 2 * kh.numel() * 2 + len(slots) * 8
+
+
+# ----------------------------------------------------------- CPU baseline ---
+
+def cpu_threads() -> int:
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_decode_sample(hk, hv, nb, kvh, bs, hd, table, lens, qh, q, budget_s: float = 15.0):
+    """Times the reference CPU path (gather + reference_attention per request,
+    one std::thread per request slice) on the sample; returns
+    (KV GB/s, seconds, kind, threads, requests used, outputs)."""
+    import oracle
+
+    threads = cpu_threads()
+    use_ref = oracle.ref() is not None
+    fn = oracle.ref_decode_batch if use_ref else None
+
+    def run(count):
+        t = time.perf_counter()
+        if use_ref:
+            out = oracle.ref_decode_batch(hk, hv, 1, kvh, bs, hd, table, lens, qh, q, first=0, count=count,
+                                          threads=min(threads, count))
+        else:
+            out = oracle.decode_batch(hk, hv, 1, nb, kvh, bs, hd, table, lens, qh, q, first=0, count=count,
+                                      threads=min(threads, count))
+        return time.perf_counter() - t, out
+
+    del fn
+    # Calibrate on one request, then size the sample to the time budget.
+    t1, _ = run(1)
+    per_wave = max(t1, 1e-3)
+    waves = max(1, int(budget_s / per_wave))
+    count = min(len(lens), max(1, waves * threads))
+    secs, out = run(count)
+    kv_bytes = int(lens[:count].sum()) * kvh * hd * 2 * 2
+    return kv_bytes / secs / 1e9, secs, "reference" if use_ref else "port", min(threads, count), count, out
+
+
+# ------------------------------------------------------------- reference ---
+
+def reference_arm(args, ranks: Ranks) -> int:
+    """The reference's own CPU implementation of batch decode (its
+    reference_attention, compiled from its sources, after the gather its GPU
+    kernel does, restated on the CPU) on this box's host cores, on config 5's
+    shapes; each step is a bounded sample of requests (one per thread)."""
+    if ranks.rank != 0:
+        return 0
+    import oracle
+    from kvflux_b200 import workloads as w
+
+    cfg = w.CONFIG5
+    threads = cpu_threads()
+    lens_all = w.config_lengths(cfg).astype(np.uint64)
+    count = min(len(lens_all), threads)
+    lens = lens_all[:count]
+    kvh, qh, hd, bs = cfg["kv_heads"], cfg["q_heads"], cfg["head_size"], cfg["block_size"]
+    pages = [(int(l) + bs - 1) // bs for l in lens]
+    nb = sum(pages)
+    ids = w.permutation(cfg["seed"], np.arange(nb))
+    width = max(pages)
+    table = np.zeros((count, width), np.uint64)
+    k = 0
+    for r, p in enumerate(pages):
+        table[r, :p] = ids[k:k + p]
+        k += p
+    n = nb * kvh * bs * hd
+    hk = w.f32_to_bf16_bits(w.normal(cfg["seed"] + 1, n))
+    hv = w.f32_to_bf16_bits(w.normal(cfg["seed"] + 2, n))
+    q = w.normal(cfg["seed"] + 3, count * qh * hd)
+    kind = "reference" if oracle.ref() is not None else "port"
+
+    def step():
+        if kind == "reference":
+            oracle.ref_decode_batch(hk, hv, 1, kvh, bs, hd, table, lens, qh, q, threads=threads)
+        else:
+            oracle.decode_batch(hk, hv, 1, nb, kvh, bs, hd, table, lens, qh, q, threads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    secs = (time.perf_counter() - t) / args.steps
+    kv_bytes = int(lens.sum()) * kvh * hd * 2 * 2
+    value = kv_bytes / secs / 1e9
+    sample = (f"{count} requests of config 5 per step (lengths {int(lens.min())}..{int(lens.max())}), "
+              f"gather + reference_attention, one request per thread")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config5 decode (Llama-3-70B heads 64Q/8KV hd128 bf16), CPU sample",
+                       "global_batch": cfg["batch"], "seq_len": "U[4096,32768]", "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------- main ---
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-secondary", action="store_true", help="headline decode only")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    ranks = Ranks(args.gpus)
+    if args.impl == "reference":
+        return reference_arm(args, ranks)
+
+    import torch
+
+    import kvflux_b200 as kv
+    from kvflux_b200 import workloads as w
+
+    ranks.init_gpu()
+    world, rank = ranks.world, ranks.rank
+    peak, peak_kind = load_peak()
+
+    wl = Decode(kv, w, w.CONFIG5, rank, world)
+    pps5 = wl.pps
+    with Clocks(ranks.local) as clk:
+        per, total_ms = time_launches(wl.launch, args.steps, args.warmup, ranks)
+    ms = ranks.reduce(total_ms / args.steps, "max")
+    kv_bytes_all = ranks.reduce(float(wl.kv_bytes), "sum")
+    value = kv_bytes_all / (ms * 1e-3) / 1e9
+    kernel_ms = statistics.mean(per)
+    achieved = wl.alg_bytes / (kernel_ms * 1e-3) / 1e9
+    ratio, capture = traffic_ratio("decode_mma_kernel")
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "peak_kind": peak_kind, "traffic": (ratio * wl.alg_bytes) if ratio else None,
+                "traffic_source": capture, "algorithmic_bytes_per_launch": wl.alg_bytes,
+                "kernel_ms_per_launch": kernel_ms, "frac_of_datasheet": achieved / DATASHEET_GBS}
+
+    # Outputs of all ranks to rank 0 over NCCL, for verification only (outside the timed region).
+    finite = bool(torch.isfinite(wl.o).all().item())
+    if ranks.dist is not None:
+        gathered = [torch.empty_like(wl.o) for _ in range(world)]
+        ranks.dist.all_gather(gathered, wl.o)
+        if rank == 0:
+            full = torch.stack([g.view(wl.batch, wl.qh, wl.hd) for g in gathered], dim=1)
+            finite = bool(torch.isfinite(full).all().item()) and full.shape[1] * full.shape[2] == w.CONFIG5["q_heads"]
+        del gathered
+
+    e2e_ms, h2d, d2h_bytes = e2e_decode(kv, wl, max(3, args.steps // 4), 3)
+    e2e_ms = ranks.reduce(e2e_ms, "max")
+    e2e = {"value": kv_bytes_all / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
+           "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h_bytes * world,
+           "api": "kvflux::v2::paged_attention_batch (pinned host Q in, O out)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        sample_req = list(range(min(64, wl.batch)))
+        hk, hv, nb, table, lens, q, o_gpu = wl.host_sample(sample_req)
+        gbs, secs, kind, cores, count, out = cpu_decode_sample(hk, hv, nb, wl.kvh, wl.bs, wl.hd, table, lens, wl.qh, q)
+        err = float(np.abs(out[:count * wl.qh * wl.hd] - o_gpu[:count * wl.qh * wl.hd]).max())
+        cpu = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": kind,
+               "sample": f"{count} of config 5's 256 requests (gather + reference_attention), {secs:.1f} s",
+               "max_abs_err_vs_gpu": err}
+
+    secondary = {}
+    if not args.no_secondary:
+        del wl
+        torch.cuda.empty_cache()
+        wg = WriteGather(kv, w, w.CONFIG2, rank, world)
+        per_w, tot_w = time_launches(wg.write, 50, 5, ranks)
+        w_ms = ranks.reduce(tot_w / 50, "max")
+        g_ms_launch = ranks.reduce(wg.graph_write_ms(), "max")
+        e2e_w_ms, e2e_w_h2d = wg.e2e_write_ms()
+        e2e_w_ms = ranks.reduce(e2e_w_ms, "max")
+        write_bytes_all = ranks.reduce(float(wg.write_bytes), "sum")
+        per_g, tot_g = time_launches(wg.gather, 10, 3, ranks)
+        g_ms = ranks.reduce(tot_g / 10, "max")
+        gather_bytes_all = ranks.reduce(float(wg.gather_bytes), "sum")
+        secondary["kv_write"] = {
+            "workload": "config2 write: 256 new tokens (64 seqs x 4) per step, 8 KV heads x 128, bf16, odd/even pool",
+            "tokens_per_s": wg.n / (w_ms * 1e-3), "ms_per_launch": w_ms,
+            "graph_tokens_per_s": wg.n / (g_ms_launch * 1e-3), "graph_ms_per_launch": g_ms_launch,
+            "graph_hbm_gbs": write_bytes_all / (g_ms_launch * 1e-3) / 1e9,
+            "graph_frac_of_peak": write_bytes_all / (g_ms_launch * 1e-3) / 1e9 / peak,
+            "e2e_tokens_per_s": wg.n / (e2e_w_ms * 1e-3), "e2e_h2d_bytes_per_step": e2e_w_h2d * world}
+        secondary["gather"] = {
+            "workload": "config2 gather: 64 seqs x 8192 tokens to contiguous K/V, one kvfx_gather_batch launch",
+            "gbs": gather_bytes_all / (g_ms * 1e-3) / 1e9, "ms_per_step": g_ms,
+            "frac_of_peak": gather_bytes_all / (g_ms * 1e-3) / 1e9 / peak}
+        del wg
+        torch.cuda.empty_cache()
+        w3 = Decode(kv, w, w.CONFIG3, rank, world)
+        per3, tot3 = time_launches(w3.launch, args.steps, args.warmup, ranks)
+        ms3 = ranks.reduce(tot3 / args.steps, "max")
+        kv3 = ranks.reduce(float(w3.kv_bytes), "sum")
+        alg3 = ranks.reduce(float(w3.alg_bytes), "sum")
+        secondary["decode_cfg3"] = {
+            "workload": "config3 decode: Llama-3-8B heads 32Q/8KV hd128 bf16, batch 64, L~U[512,8192]",
+            "kv_gbs": kv3 / (ms3 * 1e-3) / 1e9, "ms_per_step": ms3,
+            "frac_of_peak": alg3 / (ms3 * 1e-3) / 1e9 / peak}
+        del w3
+
+    clocks = clk.summary()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 K/V, FP32 Q)",
+            "config": {"workload": "config5 decode: Llama-3-70B heads 64Q/8KV hd128 bf16, batch 256, "
+                                   "L~U[4096,32768], block 16, random-fragmented pools, KV heads sharded over ranks",
+                       "global_batch": w.CONFIG5["batch"], "seq_len": "U[4096,32768]",
+                       "parallelism": f"kv-head shard x{world}", "l2": "inputs larger than L2 (no flush)",
+                       "pages_per_split": pps5},
+            "frac_of_measured_hbm": value / peak, "frac_of_datasheet_hbm": value / DATASHEET_GBS,
+            "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": args.steps,
+            "clocks": clocks, "outputs_finite": finite, "secondary": secondary,
+        }
+        print(json.dumps(line), flush=True)
+    ranks.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

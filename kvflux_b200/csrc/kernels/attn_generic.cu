@@ -53,6 +53,10 @@ __global__ void __launch_bounds__(kWarps * 32) attn_generic_kernel(const Generic
     if (p.lens != nullptr) {
         visible = p.lens[u];
         brow = p.blocks + u * p.row_stride;
+        if (visible == 0 || visible > p.row_stride * p.bs) {  // outside the table row: refuse
+            if (lane == 0) raise_flag(p.status, KVFX_FLAG_BAD_INDEX);
+            return;
+        }
     } else {
         visible = p.kv_tokens - p.units + u + 1;
         brow = p.blocks;

@@ -122,6 +122,10 @@ __global__ void __launch_bounds__(256) gather_simt_kernel(
         if (threadIdx.x == 0 && blockIdx.x == 0) raise_flag(status, KVFX_FLAG_BAD_INDEX);
         return;
     }
+    if (ceil_div(len, bs) > max_blocks) {  // length beyond the table row
+        if (threadIdx.x == 0 && blockIdx.x == 0) raise_flag(status, KVFX_FLAG_BAD_INDEX);
+        return;
+    }
     const uint64_t total = len * heads * vpr;
     const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
     for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -192,6 +196,10 @@ __global__ void __launch_bounds__(32) gather_tma_kernel(
         return;
     }
     const uint64_t pages = ceil_div(len, bs);
+    if (pages > max_blocks) {  // length beyond the table row
+        if (lane == 0 && blockIdx.x == 0) raise_flag(status, KVFX_FLAG_BAD_INDEX);
+        return;
+    }
     const uint64_t units = pages * heads;
     const uint64_t first = blockIdx.x;
     const uint64_t step = gridDim.x;
@@ -299,7 +307,8 @@ cudaError_t launch_gather(const CacheView& c, const GatherArgs& a, unsigned* sta
     if (a.batch == 0 || a.max_len == 0) return cudaSuccess;
     // TMA path: rows must be whole 16-byte runs and both chunks of a stage fit.
     const bool single = a.k_out_list == nullptr;
-    bool tma = c.row_bytes % 16 == 0 && c.chunk_bytes <= 32768;
+    bool tma = c.row_bytes % 16 == 0 && c.chunk_bytes <= 32768 &&
+               (reinterpret_cast<uintptr_t>(c.k) | reinterpret_cast<uintptr_t>(c.v)) % 16 == 0;
     if (tma && single) {
         tma = reinterpret_cast<uintptr_t>(a.k_out) % 16 == 0 &&
               reinterpret_cast<uintptr_t>(a.v_out) % 16 == 0;
@@ -310,12 +319,12 @@ cudaError_t launch_gather(const CacheView& c, const GatherArgs& a, unsigned* sta
         const uint32_t stages = static_cast<uint32_t>(
             std::min<uint64_t>(kGatherMaxStages, std::max<uint64_t>(2, 65536 / (2 * c.chunk_bytes))));
         const size_t smem = static_cast<size_t>(stages) * 2 * c.chunk_bytes;
-        static bool attr_set = false;  // per-process; the attribute is per function
-        if (!attr_set) {
+        static bool attr_set[64] = {false};  // the attribute is set once per device
+        if (c.device < 0 || c.device >= 64 || !attr_set[c.device]) {
             cudaError_t e = cudaFuncSetAttribute(gather_tma_kernel,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, 98304);
             if (e != cudaSuccess) return e;
-            attr_set = true;
+            if (c.device >= 0 && c.device < 64) attr_set[c.device] = true;
         }
         const uint64_t units_max = ceil_div(a.max_len, c.bs) * c.heads;
         const int sms = device_sm_count(c.device);

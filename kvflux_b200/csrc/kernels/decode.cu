@@ -97,7 +97,7 @@ decode_mma_kernel(const __grid_constant__ DecodeParams p, const __grid_constant_
     const uint64_t npages = ceil_div(len, 16);
     const uint32_t nsplits = static_cast<uint32_t>(ceil_div(npages, p.pages_per_split));
     if (len == 0 || split >= nsplits) return;
-    if (nsplits > p.max_splits) {  // lengths beyond the host's bound: refuse
+    if (nsplits > p.max_splits || npages > p.max_blocks) {  // length beyond the host's bounds: refuse
         if (tid == 0) raise_flag(p.status, KVFX_FLAG_BAD_INDEX);
         return;
     }

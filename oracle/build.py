@@ -1,0 +1,84 @@
+"""Builds the test oracles (TEST INFRASTRUCTURE ONLY).
+
+  oracle/libkvoracle.so        - kvoracle.c, the CPU restatement of the path
+  oracle/_ref/libkvflux_ref.so - the reference's own CPU sources (control plane
+                                 and reference_attention) + ref_shim.cpp, built
+                                 from the reference checkout when one is present
+                                 (KVFLUX_REFERENCE, default: the checkout mounted
+                                 next to this repository in the build container).
+                                 The built file travels with the tree; the
+                                 sources are never copied into it.
+
+Usage: python oracle/build.py [--force]
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+ORACLE_LIB = HERE / "libkvoracle.so"
+REF_DIR = HERE / "_ref"
+REF_LIB = REF_DIR / "libkvflux_ref.so"
+REF_SOURCES = [
+    "src/block_manager.cpp",
+    "src/physical_block_pool.cpp",
+    "src/v2/block_table.cpp",
+    "src/v2/sequence_state.cpp",
+    "src/v2/batch_block_table.cpp",
+    "src/v2/slot_mapping.cpp",
+    "src/v2/paged_kv_layout.cpp",
+    "src/v2/reference_attention.cpp",
+    "src/v2/prefix_cache.cpp",
+    "src/v2/paged_kv_read_table.cpp",
+]
+
+
+def reference_root() -> Path:
+    return Path(os.environ.get("KVFLUX_REFERENCE", "/root/reference"))
+
+
+def _run(cmd: list[str]) -> None:
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(f"oracle build failed: {' '.join(cmd)}\n{proc.stdout}\n{proc.stderr}")
+
+
+def _stale(out: Path, inputs: list[Path]) -> bool:
+    return not out.exists() or out.stat().st_mtime < max(p.stat().st_mtime for p in inputs)
+
+
+def build(force: bool = False) -> dict:
+    built = {}
+    srcs = [HERE / "kvoracle.c", HERE / "kvoracle.h"]
+    if force or _stale(ORACLE_LIB, srcs):
+        _run(["gcc", "-std=c11", "-O2", "-fPIC", "-shared", "-pthread", "-Wall", str(HERE / "kvoracle.c"),
+              "-o", str(ORACLE_LIB), "-lm"])
+    built["oracle"] = str(ORACLE_LIB)
+    ref = reference_root()
+    if (ref / "src" / "v2" / "reference_attention.cpp").exists():
+        inputs = [ref / s for s in REF_SOURCES] + [HERE / "ref_shim.cpp"]
+        if force or _stale(REF_LIB, inputs):
+            REF_DIR.mkdir(exist_ok=True)
+            _run(["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-fvisibility=hidden", "-pthread",
+                  f"-I{ref / 'include'}", *map(str, inputs), "-o", str(REF_LIB)])
+        built["reference"] = str(REF_LIB)
+    elif REF_LIB.exists():
+        built["reference"] = str(REF_LIB)  # prebuilt elsewhere, shipped with the tree
+    return built
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--force", action="store_true")
+    args = ap.parse_args(argv)
+    for k, v in build(force=args.force).items():
+        print(f"{k}: {v}")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

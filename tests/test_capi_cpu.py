@@ -1,0 +1,77 @@
+"""C-ABI checks that need no GPU: the library loads, exports every function
+include/kvfx.h declares, and rejects bad arguments before touching CUDA."""
+import ctypes
+import re
+from pathlib import Path
+
+import kvflux_b200 as kv
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "kvfx.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^(?:const char\*|int|uint64_t|uint32_t)\s+(kvfx_\w+)\(", text, re.M)))
+
+
+def test_every_declared_symbol_is_exported():
+    names = declared_functions()
+    assert len(names) >= 12
+    for name in names:
+        assert hasattr(kv.lib, name), name
+    assert set(names) == set(kv.KVFX_SYMBOLS)
+
+
+def test_version_string():
+    assert kv.lib.kvfx_version().decode().startswith("kvflux-b200")
+
+
+def _cache(**kw):
+    d = dict(k_base=4096, v_base=8192, num_blocks=4, num_kv_heads=2, block_size=16, head_size=8, dtype=kv.KVFX_BF16,
+             device=0, reserved=0)
+    d.update(kw)
+    return kv.KvfxCache(**d)
+
+
+def test_bad_descriptors_rejected_before_cuda():
+    assert kv.lib.kvfx_write(None, None, None, None, 1, None) == kv.KVFX_EINVAL
+    assert kv.lib.kvfx_write(ctypes.byref(_cache(num_blocks=0)), None, None, None, 1, None) == kv.KVFX_EINVAL
+    assert kv.lib.kvfx_write(ctypes.byref(_cache(dtype=7)), None, None, None, 1, None) == kv.KVFX_EINVAL
+    assert kv.lib.kvfx_write(ctypes.byref(_cache(reserved=1)), None, None, None, 1, None) == kv.KVFX_EINVAL
+    assert kv.lib.kvfx_write(ctypes.byref(_cache(k_base=None)), None, None, None, 1, None) == kv.KVFX_EINVAL
+    assert kv.lib.kvfx_write(ctypes.byref(_cache(num_blocks=2**63, head_size=2**31)), 1, 1, 1, 1, None) \
+        == kv.KVFX_EOVERFLOW
+    kv.lib.kvfx_write(ctypes.byref(_cache(reserved=1)), None, None, None, 1, None)
+    assert b"reserved" in kv.lib.kvfx_last_error()
+
+
+def test_empty_calls_return_ok_without_pointers():
+    c = ctypes.byref(_cache())
+    assert kv.lib.kvfx_write(c, None, None, None, 0, None) == kv.KVFX_OK
+    assert kv.lib.kvfx_gather(c, None, 0, None, None, None) == kv.KVFX_OK
+    assert kv.lib.kvfx_gather_batch(c, None, None, 0, 0, None, None, None) == kv.KVFX_OK
+    assert kv.lib.kvfx_decode(c, None, None, None, None, 0, 0, 8, 0, 0, None, 0, None) == kv.KVFX_OK
+    assert kv.lib.kvfx_attention(c, None, None, None, 0, 5, 4, None, 0, None) == kv.KVFX_OK
+
+
+def test_argument_errors():
+    c = ctypes.byref(_cache())
+    assert kv.lib.kvfx_write(c, None, 1, 1, 3, None) == kv.KVFX_EINVAL
+    assert kv.lib.kvfx_gather(c, 1, 3, None, 1, None) == kv.KVFX_EINVAL
+    assert kv.lib.kvfx_decode(c, 1, 1, 1, 1, 1, 1, 3, 10, 0, None, 0, None) == kv.KVFX_EINVAL  # 3 % 2 != 0
+    assert kv.lib.kvfx_decode(c, 1, 1, 1, 1, 1, 1, 4, 100, 0, None, 0, None) == kv.KVFX_EINVAL  # table too narrow
+    assert kv.lib.kvfx_attention(c, 1, 1, 1, 6, 5, 4, None, 0, None) == kv.KVFX_EINVAL  # Lq > kv
+    assert kv.lib.kvfx_copy_page(c, 0, 4, None) == kv.KVFX_ERANGE
+    kv.lib.kvfx_decode(c, 1, 1, 1, 1, 1, 1, 3, 10, 0, None, 0, None)
+    assert b"q_heads" in kv.lib.kvfx_last_error()
+
+
+def test_workspace_sizes():
+    c = ctypes.byref(_cache(num_blocks=1024, num_kv_heads=8, head_size=128))
+    pps = kv.lib.kvfx_decode_pages_per_split(c, 64, 32, 8192, 64 * 4352)
+    assert pps >= 4 and pps % 4 == 0
+    ws = kv.lib.kvfx_decode_workspace_bytes(c, 64, 32, 8192, pps)
+    splits = -(-(8192 // 16) // pps)
+    assert ws >= 64 * 8 * splits * 8 * 130 * 4
+    # generic shapes need no workspace
+    assert kv.lib.kvfx_decode_workspace_bytes(ctypes.byref(_cache(head_size=3)), 4, 4, 100, 0) == 0
