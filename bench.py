@@ -125,7 +125,7 @@ class Clocks:
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=fd, stderr=subprocess.DEVNULL)
             os.close(fd)
         except OSError:
@@ -525,6 +525,39 @@ def reference_arm(args, ranks: Ranks) -> int:
     return 0
 
 
+# ---------------------------------------------------------- single case ---
+
+def only_case(args, ranks: Ranks, kv, w, peak: float) -> int:
+    """One kernel's case on its own (used under ncu): setup, `warmup` untimed
+    launches, `steps` timed launches, one short JSON line."""
+    import torch
+
+    if args.only in ("decode5", "decode3"):
+        cfg = dict(w.CONFIG5 if args.only == "decode5" else w.CONFIG3)
+        if args.batch:
+            cfg["batch"] = args.batch
+        wl = Decode(kv, w, cfg, ranks.rank, ranks.world)
+        per, total = time_launches(wl.launch, args.steps, args.warmup, ranks)
+        ms = total / args.steps
+        out = {"case": args.only, "batch": cfg["batch"], "ms_per_launch": ms, "kv_bytes": wl.kv_bytes,
+               "algorithmic_bytes": wl.alg_bytes, "gbs": wl.alg_bytes / (ms * 1e-3) / 1e9,
+               "pages_per_split": wl.pps}
+    else:
+        wg = WriteGather(kv, w, w.CONFIG2, ranks.rank, ranks.world)
+        fn = wg.write if args.only == "write" else wg.gather
+        per, total = time_launches(fn, args.steps, args.warmup, ranks)
+        ms = total / args.steps
+        nbytes = wg.write_bytes if args.only == "write" else wg.gather_bytes
+        out = {"case": args.only, "ms_per_launch": ms, "algorithmic_bytes": nbytes,
+               "gbs": nbytes / (ms * 1e-3) / 1e9}
+    out["frac_of_peak"] = out["gbs"] / peak
+    torch.cuda.synchronize()
+    if ranks.rank == 0:
+        print(json.dumps(out), flush=True)
+    ranks.close()
+    return 0
+
+
 # ------------------------------------------------------------------- main ---
 
 def main(argv=None) -> int:
@@ -535,6 +568,9 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="headline decode only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather"],
+                    help="run one kernel's case alone (profiling runs); prints a short JSON line")
+    ap.add_argument("--batch", type=int, default=None, help="override the decode batch (profiling runs)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -550,11 +586,13 @@ def main(argv=None) -> int:
     ranks.init_gpu()
     world, rank = ranks.world, ranks.rank
     peak, peak_kind = load_peak()
+    if args.only:
+        return only_case(args, ranks, kv, w, peak)
 
     wl = Decode(kv, w, w.CONFIG5, rank, world)
     pps5 = wl.pps
-    with Clocks(ranks.local) as clk:
-        per, total_ms = time_launches(wl.launch, args.steps, args.warmup, ranks)
+    clk = Clocks(ranks.local).__enter__()
+    per, total_ms = time_launches(wl.launch, args.steps, args.warmup, ranks)
     ms = ranks.reduce(total_ms / args.steps, "max")
     kv_bytes_all = ranks.reduce(float(wl.kv_bytes), "sum")
     value = kv_bytes_all / (ms * 1e-3) / 1e9
@@ -577,6 +615,7 @@ def main(argv=None) -> int:
         del gathered
 
     e2e_ms, h2d, d2h_bytes = e2e_decode(kv, wl, max(3, args.steps // 4), 3)
+    clk.__exit__(None, None, None)
     e2e_ms = ranks.reduce(e2e_ms, "max")
     e2e = {"value": kv_bytes_all / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
            "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h_bytes * world,
@@ -584,7 +623,7 @@ def main(argv=None) -> int:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        sample_req = list(range(min(64, wl.batch)))
+        sample_req = list(range(min(16, wl.batch)))
         hk, hv, nb, table, lens, q, o_gpu = wl.host_sample(sample_req)
         gbs, secs, kind, cores, count, out = cpu_decode_sample(hk, hv, nb, wl.kvh, wl.bs, wl.hd, table, lens, wl.qh, q)
         err = float(np.abs(out[:count * wl.qh * wl.hd] - o_gpu[:count * wl.qh * wl.hd]).max())

@@ -86,11 +86,16 @@ public:
 private:
     static constexpr std::size_t kNone = std::numeric_limits<std::size_t>::max();
     enum class State : std::uint8_t { Free, Active, Idle };
+    // What every handle check reads, packed densely: validating a large page
+    // table touches only this array.
     struct Slot {
         std::uint64_t generation = 0;
         std::size_t refs = 0;
         State state = State::Free;
         bool published = false;
+    };
+    // What only publish/lookup/eviction read.
+    struct SlotMeta {
         std::uint64_t hash = 0;
         Tokens prefix;
         std::size_t idle_prev = kNone, idle_next = kNone;
@@ -104,6 +109,7 @@ private:
     void drop_index(std::size_t id);
 
     std::vector<Slot> slots_;
+    std::vector<SlotMeta> meta_;
     std::size_t block_size_;
     Hasher hasher_;
     std::vector<std::size_t> free_stack_;  // top of stack = back()
@@ -111,5 +117,21 @@ private:
     std::size_t active_count_ = 0, idle_count_ = 0;
     std::unordered_map<std::uint64_t, std::vector<std::size_t>> index_;
 };
+
+// Hot-path accessors, inline so page-table builds validate each entry cheaply.
+inline const BlockManager::Slot& BlockManager::live(BlockHandle h) const {
+    if (h.id >= slots_.size()) throw std::invalid_argument("block handle id out of range");
+    const Slot& s = slots_[h.id];
+    if (s.state == State::Free || s.generation != h.generation) {
+        throw std::invalid_argument("stale or released block handle");
+    }
+    return s;
+}
+
+inline BlockManager::Slot& BlockManager::live(BlockHandle h) {
+    return const_cast<Slot&>(static_cast<const BlockManager*>(this)->live(h));
+}
+
+inline std::size_t BlockManager::ref_count(BlockHandle h) const { return live(h).refs; }
 
 } // namespace kvflux

@@ -43,4 +43,17 @@ private:
     BlockManager manager_;
 };
 
+inline PhysicalBlockID PhysicalBlockPool::id(PhysicalBlockHandle handle) const {
+    // ref_count validates range, liveness and generation; an idle cached page
+    // (zero references) must not be addressed through a stale holder either.
+    if (manager_.ref_count(handle) == 0) {
+        throw std::invalid_argument("physical page has no live reference");
+    }
+    return handle.id;
+}
+
+inline std::size_t PhysicalBlockPool::ref_count(PhysicalBlockHandle handle) const {
+    return manager_.ref_count(handle);
+}
+
 } // namespace kvflux

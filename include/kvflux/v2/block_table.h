@@ -54,4 +54,8 @@ private:
     std::vector<PhysicalBlockHandle> entries_;
 };
 
+inline PhysicalBlockID BlockTable::physical_id(std::size_t logical_block) const {
+    return pool_->id(entries_.at(logical_block));  // generation-checked
+}
+
 } // namespace kvflux::v2

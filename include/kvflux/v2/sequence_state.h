@@ -62,4 +62,8 @@ private:
     BlockTable table_;
 };
 
+inline PhysicalBlockID SequenceState::physical_block_id(std::size_t logical_block) const {
+    return table_.physical_id(logical_block);
+}
+
 } // namespace kvflux::v2

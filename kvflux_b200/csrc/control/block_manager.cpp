@@ -9,7 +9,7 @@
 namespace kvflux {
 
 BlockManager::BlockManager(std::size_t capacity, std::size_t block_size, Hasher hasher)
-    : slots_(capacity), block_size_(block_size), hasher_(std::move(hasher)) {
+    : slots_(capacity), meta_(capacity), block_size_(block_size), hasher_(std::move(hasher)) {
     if (capacity == 0 || block_size == 0 || !hasher_) {
         throw std::invalid_argument("block manager needs a positive capacity, block size and a hasher");
     }
@@ -18,50 +18,37 @@ BlockManager::BlockManager(std::size_t capacity, std::size_t block_size, Hasher 
     for (std::size_t i = 0; i < capacity; ++i) free_stack_[i] = capacity - 1 - i;
 }
 
-const BlockManager::Slot& BlockManager::live(BlockHandle h) const {
-    if (h.id >= slots_.size()) throw std::invalid_argument("block handle id out of range");
-    const Slot& s = slots_[h.id];
-    if (s.state == State::Free || s.generation != h.generation) {
-        throw std::invalid_argument("stale or released block handle");
-    }
-    return s;
-}
-
-BlockManager::Slot& BlockManager::live(BlockHandle h) {
-    return const_cast<Slot&>(static_cast<const BlockManager*>(this)->live(h));
-}
-
 void BlockManager::idle_push(std::size_t id) noexcept {
-    Slot& s = slots_[id];
+    SlotMeta& s = meta_[id];
     s.idle_prev = idle_newest_;
     s.idle_next = kNone;
     if (idle_newest_ == kNone) idle_oldest_ = id;
-    else slots_[idle_newest_].idle_next = id;
+    else meta_[idle_newest_].idle_next = id;
     idle_newest_ = id;
     ++idle_count_;
 }
 
 void BlockManager::idle_remove(std::size_t id) noexcept {
-    Slot& s = slots_[id];
+    SlotMeta& s = meta_[id];
     if (s.idle_prev == kNone) idle_oldest_ = s.idle_next;
-    else slots_[s.idle_prev].idle_next = s.idle_next;
+    else meta_[s.idle_prev].idle_next = s.idle_next;
     if (s.idle_next == kNone) idle_newest_ = s.idle_prev;
-    else slots_[s.idle_next].idle_prev = s.idle_prev;
+    else meta_[s.idle_next].idle_prev = s.idle_prev;
     s.idle_prev = s.idle_next = kNone;
     --idle_count_;
 }
 
 void BlockManager::drop_index(std::size_t id) {
-    Slot& s = slots_[id];
-    auto bucket = index_.find(s.hash);
+    SlotMeta& m = meta_[id];
+    auto bucket = index_.find(m.hash);
     if (bucket != index_.end()) {
         auto& ids = bucket->second;
         ids.erase(std::remove(ids.begin(), ids.end(), id), ids.end());
         if (ids.empty()) index_.erase(bucket);
     }
-    s.published = false;
-    s.prefix.clear();
-    s.prefix.shrink_to_fit();
+    slots_[id].published = false;
+    m.prefix.clear();
+    m.prefix.shrink_to_fit();
 }
 
 BlockHandle BlockManager::allocate() {
@@ -116,8 +103,6 @@ void BlockManager::release(BlockHandle h) {
     }
 }
 
-std::size_t BlockManager::ref_count(BlockHandle h) const { return live(h).refs; }
-
 bool BlockManager::is_published(BlockHandle h) const { return live(h).published; }
 
 void BlockManager::publish(BlockHandle h, const Tokens& prefix) {
@@ -129,7 +114,7 @@ void BlockManager::publish(BlockHandle h, const Tokens& prefix) {
     auto bucket = index_.find(hash);
     if (bucket != index_.end()) {
         for (std::size_t other : bucket->second) {
-            if (slots_[other].prefix == prefix) {
+            if (meta_[other].prefix == prefix) {
                 throw std::invalid_argument("prefix is already published");
             }
         }
@@ -143,8 +128,8 @@ void BlockManager::publish(BlockHandle h, const Tokens& prefix) {
         if (inserted) index_.erase(it);
         throw;
     }
-    s.prefix = std::move(stored);
-    s.hash = hash;
+    meta_[h.id].prefix = std::move(stored);
+    meta_[h.id].hash = hash;
     s.published = true;
 }
 
@@ -153,9 +138,8 @@ bool BlockManager::lookup(const Tokens& prefix, BlockHandle& out) {
     auto bucket = index_.find(hasher_(prefix));
     if (bucket == index_.end()) return false;
     for (std::size_t id : bucket->second) {
-        const Slot& s = slots_[id];
-        if (s.prefix != prefix) continue;  // same hash, different tokens
-        const BlockHandle hit{id, s.generation};
+        if (meta_[id].prefix != prefix) continue;  // same hash, different tokens
+        const BlockHandle hit{id, slots_[id].generation};
         retain(hit);
         out = hit;
         return true;

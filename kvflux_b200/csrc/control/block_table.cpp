@@ -63,10 +63,6 @@ void BlockTable::append_shared(const BlockTable& source, std::size_t logical_blo
     append_existing(h);
 }
 
-PhysicalBlockID BlockTable::physical_id(std::size_t logical_block) const {
-    return pool_->id(entries_.at(logical_block));
-}
-
 PhysicalBlockHandle BlockTable::handle(std::size_t logical_block) const {
     const PhysicalBlockHandle h = entries_.at(logical_block);
     (void)pool_->id(h);

@@ -21,16 +21,6 @@ bool PhysicalBlockPool::lookup(const Tokens& prefix, PhysicalBlockHandle& out) {
 }
 bool PhysicalBlockPool::is_published(PhysicalBlockHandle h) const { return manager_.is_published(h); }
 
-PhysicalBlockID PhysicalBlockPool::id(PhysicalBlockHandle h) const {
-    // ref_count validates range, liveness and generation; an idle cached page
-    // (zero references) must not be addressed through a stale holder either.
-    if (manager_.ref_count(h) == 0) {
-        throw std::invalid_argument("physical page has no live reference");
-    }
-    return h.id;
-}
-
-std::size_t PhysicalBlockPool::ref_count(PhysicalBlockHandle h) const { return manager_.ref_count(h); }
 std::size_t PhysicalBlockPool::capacity() const noexcept { return manager_.capacity(); }
 std::size_t PhysicalBlockPool::block_size() const noexcept { return manager_.block_size(); }
 std::size_t PhysicalBlockPool::available() const noexcept {

@@ -107,10 +107,6 @@ void SequenceState::drop_last_full_block() noexcept {
     num_tokens_ = num_tokens_ >= block_size_ ? num_tokens_ - block_size_ : 0;
 }
 
-PhysicalBlockID SequenceState::physical_block_id(std::size_t logical_block) const {
-    return table_.physical_id(logical_block);
-}
-
 PhysicalBlockHandle SequenceState::block_handle(std::size_t logical_block) const {
     return table_.handle(logical_block);
 }

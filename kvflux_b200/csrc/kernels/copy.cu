@@ -166,13 +166,13 @@ cudaError_t gather_simt_vb(const CacheView& c, const GatherArgs& a, unsigned* st
 // ------------------------------------------------------------- gather (TMA) ---
 // Unit = one head of one page: a contiguous chunk [bs][head_size] in K and in
 // V. One warp per CTA runs an S-stage ring: lane 0 brings a unit's K and V
-// chunks into shared memory with two bulk (TMA) loads completing on the
-// stage's mbarrier; then every lane writes rows of that unit back out with
-// bulk shared->global copies (row t of the chunk is token j*bs+t, head h of
-// the output), so the (head, token) -> (token, head) transpose is done by the
-// copy engine with 16-byte aligned row runs. A stage is refilled once the bulk
-// stores reading it have finished (cp.async.bulk.wait_group.read).
+// chunks into shared memory with two bulk (TMA) loads that complete on the
+// stage's mbarrier; then the 32 lanes write the chunk's rows out with 16-byte
+// stores (row t of the chunk is token j*bs+t, head h, of the output; a row is
+// written by consecutive lanes, so each row is one coalesced run), and lane 0
+// refills the stage with the unit S iterations ahead.
 constexpr int kGatherMaxStages = 8;
+constexpr int kGatherCtasPerSm = 6;
 
 __global__ void __launch_bounds__(32) gather_tma_kernel(
     const char* __restrict__ k_cache, const char* __restrict__ v_cache,
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(32) gather_tma_kernel(
     char* k_out = static_cast<char*>(k_list != nullptr ? k_list[b] : k_one);
     char* v_out = static_cast<char*>(v_list != nullptr ? v_list[b] : v_one);
     if (((reinterpret_cast<uintptr_t>(k_out) | reinterpret_cast<uintptr_t>(v_out)) & 15u) != 0) {
-        // Bulk copies need 16-byte aligned global addresses.
+        // 16-byte stores need 16-byte aligned outputs (batched ones are only known here).
         if (lane == 0 && blockIdx.x == 0) raise_flag(status, KVFX_FLAG_BAD_INDEX);
         return;
     }
@@ -204,13 +204,8 @@ __global__ void __launch_bounds__(32) gather_tma_kernel(
     const uint64_t first = blockIdx.x;
     const uint64_t step = gridDim.x;
     if (first >= units) return;
+    const uint32_t vpr = row_bytes / 16;  // 16-byte vectors per row
 
-    unsigned char* stage_k[kGatherMaxStages];
-    unsigned char* stage_v[kGatherMaxStages];
-    for (uint32_t st = 0; st < stages; ++st) {
-        stage_k[st] = smem + static_cast<size_t>(2 * st) * chunk_bytes;
-        stage_v[st] = stage_k[st] + chunk_bytes;
-    }
     if (lane == 0) {
         for (uint32_t st = 0; st < stages; ++st) mbar_init(&full[st], 1);
         fence_mbarrier_init();
@@ -230,9 +225,10 @@ __global__ void __launch_bounds__(32) gather_tma_kernel(
         }
         const uint64_t off = (blk * heads + h) * static_cast<uint64_t>(chunk_bytes);
         const uint32_t st = static_cast<uint32_t>(it % stages);
+        unsigned char* sk = smem + static_cast<size_t>(2 * st) * chunk_bytes;
         mbar_arrive_expect_tx(&full[st], 2 * chunk_bytes);
-        bulk_g2s(stage_k[st], k_cache + off, chunk_bytes, &full[st]);
-        bulk_g2s(stage_v[st], v_cache + off, chunk_bytes, &full[st]);
+        bulk_g2s(sk, k_cache + off, chunk_bytes, &full[st]);
+        bulk_g2s(sk + chunk_bytes, v_cache + off, chunk_bytes, &full[st]);
     };
 
     if (lane == 0) {
@@ -248,21 +244,24 @@ __global__ void __launch_bounds__(32) gather_tma_kernel(
         const uint64_t h = u - j * heads;
         const uint64_t t0 = j * bs;
         const uint32_t rows = static_cast<uint32_t>(umin64(bs, len - t0));
-        for (uint32_t t = lane; t < rows; t += 32) {
-            const uint64_t dst = ((t0 + t) * heads + h) * static_cast<uint64_t>(row_bytes);
-            bulk_s2g(k_out + dst, stage_k[st] + static_cast<size_t>(t) * row_bytes, row_bytes);
-            bulk_s2g(v_out + dst, stage_v[st] + static_cast<size_t>(t) * row_bytes, row_bytes);
+        const uint4* sk = reinterpret_cast<const uint4*>(smem + static_cast<size_t>(2 * st) * chunk_bytes);
+        const uint4* sv = sk + chunk_bytes / 16;
+        const uint32_t n = rows * vpr;
+        for (uint32_t i = lane; i < n; i += 32) {
+            const uint32_t t = i / vpr;
+            const uint32_t c = i - t * vpr;
+            const uint64_t dst = ((t0 + t) * heads + h) * static_cast<uint64_t>(row_bytes) + c * 16u;
+            const uint4 kx = sk[i];
+            const uint4 vx = sv[i];
+            __stcs(reinterpret_cast<uint4*>(k_out + dst), kx);
+            __stcs(reinterpret_cast<uint4*>(v_out + dst), vx);
         }
-        bulk_commit();
-        if (it >= 1) {
-            // The stores of iteration it-1 have finished reading their stage:
-            // refill it with iteration it-1+stages.
-            bulk_wait_read<1>();
-            __syncwarp();
-            if (lane == 0) issue(it - 1 + stages);
+        __syncwarp();  // every lane has read the stage
+        if (lane == 0) {
+            fence_proxy_async_smem();  // order those reads before the refill's async writes
+            issue(it + stages);
         }
     }
-    bulk_wait_all<0>();
 }
 
 }  // namespace
@@ -317,18 +316,18 @@ cudaError_t launch_gather(const CacheView& c, const GatherArgs& a, unsigned* sta
     // alignment of the row size; the entry point verifies pointer alignment.
     if (tma) {
         const uint32_t stages = static_cast<uint32_t>(
-            std::min<uint64_t>(kGatherMaxStages, std::max<uint64_t>(2, 65536 / (2 * c.chunk_bytes))));
+            std::min<uint64_t>(kGatherMaxStages, std::max<uint64_t>(2, 32768 / (2 * c.chunk_bytes))));
         const size_t smem = static_cast<size_t>(stages) * 2 * c.chunk_bytes;
         static bool attr_set[64] = {false};  // the attribute is set once per device
         if (c.device < 0 || c.device >= 64 || !attr_set[c.device]) {
             cudaError_t e = cudaFuncSetAttribute(gather_tma_kernel,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 98304);
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 131072);
             if (e != cudaSuccess) return e;
             if (c.device >= 0 && c.device < 64) attr_set[c.device] = true;
         }
         const uint64_t units_max = ceil_div(a.max_len, c.bs) * c.heads;
         const int sms = device_sm_count(c.device);
-        const uint64_t ctas_total = static_cast<uint64_t>(sms) * 3;
+        const uint64_t ctas_total = static_cast<uint64_t>(sms) * kGatherCtasPerSm;
         const uint64_t per_seq = std::max<uint64_t>(1, ctas_total / a.batch);
         const uint32_t gx = static_cast<uint32_t>(std::min<uint64_t>(units_max, per_seq));
         dim3 grid(gx, static_cast<uint32_t>(a.batch));

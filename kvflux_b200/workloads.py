@@ -83,11 +83,15 @@ def encode(x: np.ndarray, dtype: str) -> np.ndarray:
 
 
 def decode(raw: np.ndarray, dtype: str) -> np.ndarray:
+    """Raw cache elements (bit patterns or floats) -> float32 values."""
+    raw = np.asarray(raw)
     if dtype == "bfloat16":
         return bf16_bits_to_f32(raw)
     if dtype == "float16":
-        return np.asarray(raw, np.uint16).view(np.float16).astype(np.float32)
-    return np.asarray(raw, np.float32)
+        return raw.astype(np.uint16).view(np.float16).astype(np.float32)
+    if raw.dtype in (np.uint32, np.int32):
+        return raw.view(np.float32)
+    return raw.astype(np.float32)
 
 
 DTYPES = {"float16": _C.DType.Float16, "bfloat16": _C.DType.BFloat16, "float32": _C.DType.Float32}

@@ -55,8 +55,12 @@ def u64(a):
 
 
 def call(fn, *args):
-    rc = fn(*args)
+    """Calls a C-ABI entry point; tensor arguments pass their device address and
+    stay referenced (alive) until the launch has completed."""
+    keep = [a for a in args if isinstance(a, torch.Tensor)]
+    rc = fn(*[a.data_ptr() if isinstance(a, torch.Tensor) else a for a in args])
     torch.cuda.synchronize()
+    del keep
     kv.check(rc, fn.__name__)
 
 
@@ -75,7 +79,7 @@ def test_write_byte_exact(dtype, hd, bs, heads):
     kn = w.encode(w.normal(21, n * heads * hd), dtype).view(np.uint8)
     vn = w.encode(w.normal(22, n * heads * hd), dtype).view(np.uint8)
     dk, dv = torch.from_numpy(kn.copy()).cuda(), torch.from_numpy(vn.copy()).cuda()
-    call(kv.lib.kvfx_write, ctypes.byref(c.desc), dk.data_ptr(), dv.data_ptr(), u64(slots).data_ptr(), n, None)
+    call(kv.lib.kvfx_write, ctypes.byref(c.desc), dk.data_ptr(), dv.data_ptr(), u64(slots), n, None)
     oracle.write(c.host_k, c.host_v, c.nb, heads, bs, c.row, kn, vn, slots)
     gk, gv = c.device_bytes()
     assert np.array_equal(gk, c.host_k) and np.array_equal(gv, c.host_v)
@@ -92,7 +96,7 @@ def test_gather_byte_exact_with_sentinel(dtype, hd, bs, heads, length):
     out_bytes = length * heads * c.row
     ko = torch.full((out_bytes + 64,), 0xA5, dtype=torch.uint8, device="cuda")
     vo = torch.full((out_bytes + 64,), 0xA5, dtype=torch.uint8, device="cuda")
-    call(kv.lib.kvfx_gather, ctypes.byref(c.desc), u64(blocks).data_ptr(), length, ko.data_ptr(), vo.data_ptr(),
+    call(kv.lib.kvfx_gather, ctypes.byref(c.desc), u64(blocks), length, ko.data_ptr(), vo.data_ptr(),
          None)
     ek, ev = oracle.gather(c.host_k, c.host_v, c.nb, heads, bs, c.row, blocks, length)
     gk, gv = ko.cpu().numpy(), vo.cpu().numpy()
@@ -117,7 +121,7 @@ def test_gather_batch_byte_exact(dtype, hd):
     outs_v = [torch.full_like(t, 0xA5) for t in outs_k]
     pk = u64(np.array([t.data_ptr() for t in outs_k], np.uint64))
     pv = u64(np.array([t.data_ptr() for t in outs_v], np.uint64))
-    call(kv.lib.kvfx_gather_batch, ctypes.byref(c.desc), u64(table).data_ptr(), u64(lens).data_ptr(), len(lens),
+    call(kv.lib.kvfx_gather_batch, ctypes.byref(c.desc), u64(table), u64(lens), len(lens),
          width, pk.data_ptr(), pv.data_ptr(), None)
     for r, l in enumerate(lens):
         l = int(l)
@@ -186,8 +190,8 @@ def test_decode_matches_oracle(dtype, hd, bs, kvh, group):
     qd = torch.from_numpy(q).cuda()
     out = torch.full((batch * qh * hd + 1,), 12345.0, device="cuda")
     for _ in range(2):  # the second call reuses the workspace (counters must have been reset)
-        call(kv.lib.kvfx_decode, ctypes.byref(c.desc), qd.data_ptr(), out.data_ptr(), u64(table).data_ptr(),
-             u64(lens_np).data_ptr(), batch, table.shape[1], qh, max_len, 0, ws.data_ptr(), ws.numel(), None)
+        call(kv.lib.kvfx_decode, ctypes.byref(c.desc), qd.data_ptr(), out.data_ptr(), u64(table),
+             u64(lens_np), batch, table.shape[1], qh, max_len, 0, ws.data_ptr(), ws.numel(), None)
         got = out.cpu().numpy()
         exp = oracle.decode_batch(c.host_k, c.host_v, w.DTYPE_CODE[dtype], c.nb, kvh, bs, hd, table, lens_np, qh, q,
                                   threads=8)
@@ -207,8 +211,8 @@ def test_decode_split_k_merge(pps):
     ws = torch.zeros(max(int(ws_bytes), 16), dtype=torch.uint8, device="cuda")
     qd = torch.from_numpy(q).cuda()
     out = torch.empty(batch * qh * 128, device="cuda")
-    call(kv.lib.kvfx_decode, ctypes.byref(c.desc), qd.data_ptr(), out.data_ptr(), u64(table).data_ptr(),
-         u64(lens_np).data_ptr(), batch, table.shape[1], qh, max_len, pps, ws.data_ptr(), ws.numel(), None)
+    call(kv.lib.kvfx_decode, ctypes.byref(c.desc), qd.data_ptr(), out.data_ptr(), u64(table),
+         u64(lens_np), batch, table.shape[1], qh, max_len, pps, ws.data_ptr(), ws.numel(), None)
     exp = oracle.decode_batch(c.host_k, c.host_v, 1, c.nb, 4, 16, 128, table, lens_np, qh, q, threads=8)
     assert float(np.abs(out.cpu().numpy() - exp).max()) < TOL["bfloat16"]
 
@@ -224,7 +228,7 @@ def test_attention_single_sequence(dtype, hd, bs, kvh, group, lq, kvlen):
     ws = torch.zeros(max(int(ws_bytes), 16), dtype=torch.uint8, device="cuda")
     qd = torch.from_numpy(q).cuda()
     out = torch.full((lq * qh * hd + 1,), 12345.0, device="cuda")
-    call(kv.lib.kvfx_attention, ctypes.byref(c.desc), qd.data_ptr(), out.data_ptr(), u64(blocks).data_ptr(), lq,
+    call(kv.lib.kvfx_attention, ctypes.byref(c.desc), qd.data_ptr(), out.data_ptr(), u64(blocks), lq,
          kvlen, qh, ws.data_ptr(), ws.numel(), None)
     exp = oracle.attention_rows(c.host_k, c.host_v, w.DTYPE_CODE[dtype], c.nb, kvh, bs, hd, blocks, lq, kvlen, qh, q,
                                 threads=8)
@@ -238,11 +242,11 @@ def test_out_of_range_ids_are_flagged_not_followed():
     bad = np.array([1, 99], np.uint64)  # page 99 does not exist
     ko = torch.zeros(8 * 2 * 8, dtype=torch.float32, device="cuda")
     vo = torch.zeros_like(ko)
-    call(kv.lib.kvfx_gather, ctypes.byref(c.desc), u64(bad).data_ptr(), 8, ko.data_ptr(), vo.data_ptr(), None)
+    call(kv.lib.kvfx_gather, ctypes.byref(c.desc), u64(bad), 8, ko.data_ptr(), vo.data_ptr(), None)
     assert kv.device_status(0) & kv.KVFX_FLAG_BAD_INDEX
     slots = np.array([0, 8 * 4 + 5], np.uint64)  # second slot is beyond the cache
     kn = torch.ones(2 * 2 * 8, device="cuda")
-    call(kv.lib.kvfx_write, ctypes.byref(c.desc), kn.data_ptr(), kn.data_ptr(), u64(slots).data_ptr(), 2, None)
+    call(kv.lib.kvfx_write, ctypes.byref(c.desc), kn.data_ptr(), kn.data_ptr(), u64(slots), 2, None)
     assert kv.device_status(0) & kv.KVFX_FLAG_BAD_INDEX
     # Only slot 0 (page 0, offset 0) changed: both of its head rows hold the new ones.
     gk, _ = c.device_bytes()
@@ -258,6 +262,7 @@ def test_workspace_too_small_is_rejected():
     need = kv.lib.kvfx_decode_workspace_bytes(ctypes.byref(c.desc), 1, 8, 1000, 4)
     assert need > 0
     q = torch.zeros(8 * 128, device="cuda")
-    rc = kv.lib.kvfx_decode(ctypes.byref(c.desc), q.data_ptr(), q.data_ptr(), u64(table).data_ptr(),
-                            u64(lens).data_ptr(), 1, 63, 8, 1000, 4, None, 0, None)
+    td, ld = u64(table), u64(lens)
+    rc = kv.lib.kvfx_decode(ctypes.byref(c.desc), q.data_ptr(), q.data_ptr(), td.data_ptr(), ld.data_ptr(), 1, 63, 8,
+                            1000, 4, None, 0, None)
     assert rc == kv.KVFX_ENOSPACE
