@@ -123,6 +123,27 @@ int kvfx_decode(const kvfx_cache* cache, const float* q, float* o,
                 void* stream);
 
 /*
+ * Batch decode that allocates nothing: the same computation and arguments as
+ * kvfx_decode without pages_per_split and the workspace. No counterpart in
+ * the reference. For callers that cannot call cudaMalloc: engines that hand
+ * all device memory to their KV pool at start-up, loops that cannot take
+ * cudaMalloc/cudaFree's implicit synchronisation, and embedders whose
+ * allocator policy forbids device allocations outside their own allocator.
+ * Its scratch (split-K partials + counters) is a static 16 MiB device array
+ * held by every GPU that loads this code until the process exits; the split
+ * size is chosen so the scratch fits, and a batch whose batch x num_kv_heads
+ * cannot fit even with one split per sequence is rejected with KVFX_ENOSPACE.
+ * The first call on a device looks up the array's address (make it before
+ * any stream capture). All calls share the array: calls that overlap on the
+ * GPU race; each call clears the counters it uses. Device-side index/timeout
+ * flags are not recorded for this entry point.
+ */
+int kvfx_decode_noalloc(const kvfx_cache* cache, const float* q, float* o,
+                        const uint64_t* block_table, const uint64_t* seq_lens, uint64_t batch,
+                        uint64_t max_blocks_per_seq, uint32_t q_heads, uint64_t max_seq_len,
+                        void* stream);
+
+/*
  * Single-sequence causal PagedAttention with query_tokens queries aligned to
  * the end of the kv_tokens-long sequence (query i sees positions
  * <= kv_tokens - query_tokens + i). q, o: device float[query_tokens][q_heads][head_size];

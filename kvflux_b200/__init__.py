@@ -1,6 +1,6 @@
 """kvflux_b200: KVFlux's v2 paged-KV data path on B200 (sm_100a).
 
-Two native surfaces, both built in-tree by ``python -m kvflux_b200.build``:
+Two native surfaces, both built in-tree by ``python kvflux_b200/build.py``:
 
 * ``kvflux_b200.lib`` - ctypes binding of the C ABI in include/kvfx.h
   (libkvflux_b200.so): stream-ordered kernels taking plain device pointers.
@@ -21,7 +21,7 @@ _LIB_PATH = _PKG / "libkvflux_b200.so"
 
 if not _LIB_PATH.exists():
     raise ImportError(
-        f"kvflux_b200 native library missing ({_LIB_PATH.name}); build it with `python -m kvflux_b200.build`")
+        f"kvflux_b200 native library missing ({_LIB_PATH.name}); build it with `python kvflux_b200/build.py`")
 
 from ._C import *  # noqa: E402,F401,F403  (the C++ v2 API)
 from . import _C  # noqa: E402
@@ -63,6 +63,7 @@ def _load():
     L.kvfx_decode_pages_per_split.argtypes = [C, u64, u32, u64, u64]
     L.kvfx_decode_pages_per_split.restype = u32
     L.kvfx_decode.argtypes = [C, vp, vp, vp, vp, u64, u64, u32, u64, u32, vp, u64, vp]
+    L.kvfx_decode_noalloc.argtypes = [C, vp, vp, vp, vp, u64, u64, u32, u64, vp]
     L.kvfx_attention_workspace_bytes.argtypes = [C, u64, u64, u32]
     L.kvfx_attention_workspace_bytes.restype = u64
     L.kvfx_attention.argtypes = [C, vp, vp, vp, u64, u64, u32, vp, u64, vp]
@@ -79,7 +80,8 @@ lib = _load()
 #: Every symbol include/kvfx.h declares (checked by the tests).
 KVFX_SYMBOLS = (
     "kvfx_write", "kvfx_gather", "kvfx_gather_batch", "kvfx_copy_page", "kvfx_decode_workspace_bytes",
-    "kvfx_decode_pages_per_split", "kvfx_decode", "kvfx_attention_workspace_bytes", "kvfx_attention",
+    "kvfx_decode_pages_per_split", "kvfx_decode", "kvfx_decode_noalloc", "kvfx_attention_workspace_bytes",
+    "kvfx_attention",
     "kvfx_last_error", "kvfx_device_status", "kvfx_version",
 )
 

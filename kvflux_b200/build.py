@@ -5,7 +5,7 @@ Outputs (next to this file, git-ignored, shipped with the tree):
                        + the C++17 v2 API (include/kvflux/...)
   _C.<abi>.so        - pybind11 binding of the C++ API
 
-Usage: python -m kvflux_b200.build [--force] [-j N]
+Usage: python kvflux_b200/build.py [--force] [-j N]
 Recompiles a source only when it, or any header of the tree, is newer than
 its object file. nvcc cross-compiles for sm_100a without a GPU.
 """

@@ -104,6 +104,10 @@ unsigned* status_word(int device) {
 
 }  // namespace
 
+namespace kvfx {
+void set_last_error(const char* msg) { g_last_error = msg; }
+}  // namespace kvfx
+
 extern "C" {
 
 const char* kvfx_last_error(void) { return g_last_error.c_str(); }

@@ -457,4 +457,27 @@ cudaError_t launch_decode(const CacheView& c, const DecodeArgs& a, unsigned* sta
                                 : launch_fast<64, __half>(c, a, maps, pps, max_splits, status, s);
 }
 
+uint64_t decode_counters_offset(const CacheView& c, uint64_t batch, uint64_t max_len, uint32_t pages_per_split) {
+    const uint32_t pps = clamp_pps(c, max_len, pages_per_split);
+    const uint64_t max_splits = ceil_div(ceil_div(std::max<uint64_t>(max_len, 1), c.bs), pps);
+    const uint64_t per = 8ull * (c.hd + 2);
+    return ((batch * c.heads * max_splits * per * 4) + 255) & ~uint64_t(255);
+}
+
+cudaError_t launch_decode_with_maps(const CacheView& c, const DecodeArgs& a, const CacheMaps& maps,
+                                    unsigned* status, cudaStream_t s) {
+    const uint32_t group = a.q_heads / c.heads;
+    if (!fast_path(c, group)) return cudaErrorInvalidValue;
+    const uint32_t pps = clamp_pps(c, a.max_len, a.pages_per_split);
+    const uint32_t max_splits =
+        static_cast<uint32_t>(ceil_div(ceil_div(std::max<uint64_t>(a.max_len, 1), c.bs), pps));
+    if (c.hd == 128) {
+        return c.dtype == KVFX_BF16
+                   ? launch_fast<128, __nv_bfloat16>(c, a, &maps, pps, max_splits, status, s)
+                   : launch_fast<128, __half>(c, a, &maps, pps, max_splits, status, s);
+    }
+    return c.dtype == KVFX_BF16 ? launch_fast<64, __nv_bfloat16>(c, a, &maps, pps, max_splits, status, s)
+                                : launch_fast<64, __half>(c, a, &maps, pps, max_splits, status, s);
+}
+
 }  // namespace kvfx

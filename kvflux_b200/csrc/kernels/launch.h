@@ -105,6 +105,17 @@ struct CacheMaps {
     bool valid;
 };
 const CacheMaps* cache_maps(const CacheView& c, cudaError_t* err);
+// Encodes the maps into caller storage (no caching, no heap allocation).
+bool encode_cache_maps(const CacheView& c, CacheMaps* out, cudaError_t* err);
+
+// Byte offset of the split counters inside a decode workspace.
+uint64_t decode_counters_offset(const CacheView& c, uint64_t batch, uint64_t max_len, uint32_t pages_per_split);
+// The batch-decode fast path with caller-provided tensor maps (16-bit caches,
+// head_size 64/128, block 16, group <= 8 only).
+cudaError_t launch_decode_with_maps(const CacheView& c, const DecodeArgs& a, const CacheMaps& maps,
+                                    unsigned* status, cudaStream_t s);
+// Records the calling thread's message for kvfx_last_error().
+void set_last_error(const char* msg);
 
 int device_sm_count(int device);
 

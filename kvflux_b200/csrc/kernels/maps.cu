@@ -84,6 +84,15 @@ const CacheMaps* cache_maps(const CacheView& c, cudaError_t* err) {
     return m;
 }
 
+bool encode_cache_maps(const CacheView& c, CacheMaps* out, cudaError_t* err) {
+    *err = cudaSuccess;
+    EncodeTiled fn = encoder(err);
+    if (fn == nullptr) return false;
+    out->valid = encode_one(fn, &out->k, c.k, c) && encode_one(fn, &out->v, c.v, c);
+    if (!out->valid) *err = cudaErrorInvalidValue;
+    return out->valid;
+}
+
 int device_sm_count(int device) {
     static int counts[64] = {0};
     if (device < 0 || device >= 64) return 148;
