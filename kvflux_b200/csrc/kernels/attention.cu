@@ -1,7 +1,8 @@
 // Single-sequence PagedAttention dispatch (paged_attention's kernel side).
 // One query token is a decode step and runs on the batch-decode kernel with
 // a batch of one; several query tokens (a causal prefill or a multi-token
-// suffix) run on the generic kernel.
+// suffix) run on the tcgen05 prefill kernel for 16-bit caches with
+// head_size 128 and block 16, and on the generic kernel otherwise.
 #include "common.cuh"
 #include "launch.h"
 
@@ -20,6 +21,7 @@ cudaError_t launch_attention(const CacheView& c, const AttentionArgs& a, unsigne
                      a.q_heads, 0, a.workspace, a.workspace_bytes};
         return launch_decode(c, d, status, s);
     }
+    if (prefill_tc_supported(c, a)) return launch_prefill_tc(c, a, status, s);
     GenericAttnArgs g{a.q, a.o, a.blocks, 0, nullptr, a.query_tokens, a.kv_tokens, a.q_heads};
     return launch_attention_generic(c, g, status, s);
 }

@@ -82,6 +82,9 @@ uint64_t attention_workspace_bytes(const CacheView& c, uint64_t query_tokens, ui
                                    uint32_t q_heads);
 cudaError_t launch_attention(const CacheView& c, const AttentionArgs& a, unsigned* status,
                              cudaStream_t s);
+// Causal prefill on tcgen05 (prefill.cu): shapes it covers, and the launch.
+bool prefill_tc_supported(const CacheView& c, const AttentionArgs& a);
+cudaError_t launch_prefill_tc(const CacheView& c, const AttentionArgs& a, unsigned* status, cudaStream_t s);
 
 // Generic SIMT attention over "query rows" (used by both entry points for the
 // shapes the specialised kernels do not cover).

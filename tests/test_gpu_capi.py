@@ -266,3 +266,47 @@ def test_workspace_too_small_is_rejected():
     rc = kv.lib.kvfx_decode(ctypes.byref(c.desc), q.data_ptr(), q.data_ptr(), td.data_ptr(), ld.data_ptr(), 1, 63, 8,
                             1000, 4, None, 0, None)
     assert rc == kv.KVFX_ENOSPACE
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("kvh,group,lq,kvlen", [(2, 4, 2, 2), (1, 8, 127, 127), (2, 1, 128, 128), (2, 4, 129, 129),
+                                                (1, 4, 300, 300), (2, 4, 100, 333), (1, 2, 64, 1000)])
+def test_prefill_tensor_core_path(dtype, kvh, group, lq, kvlen):
+    """Causal prefill on the tcgen05 kernel (16-bit cache, head_size 128,
+    block 16): suffix-aligned queries, partial query and KV tiles, NaN-poisoned
+    slots past the sequence end; max |err| against the FP64 oracle."""
+    c, table, _, _, qh = _decode_case(dtype, 128, 16, kvh, group, [kvlen], seed=lq * 7 + kvlen + group)
+    blocks = table[0]
+    q = w.normal(lq + 11 * kvlen, lq * qh * 128)
+    qd = torch.from_numpy(q).cuda()
+    out = torch.full((lq * qh * 128 + 1,), 12345.0, device="cuda")
+    call(kv.lib.kvfx_attention, ctypes.byref(c.desc), qd.data_ptr(), out.data_ptr(), u64(blocks), lq, kvlen, qh,
+         None, 0, None)
+    exp = oracle.attention_rows(c.host_k, c.host_v, w.DTYPE_CODE[dtype], c.nb, kvh, 16, 128, blocks, lq, kvlen, qh,
+                                q, threads=8)
+    got = out.cpu().numpy()
+    assert np.isfinite(got[:-1]).all()
+    err = float(np.abs(got[:-1] - exp).max())
+    assert err < TOL[dtype], err
+    assert got[-1] == 12345.0
+    assert kv.device_status(0) == 0
+
+
+def test_prefill_long_sequence_sampled_rows():
+    """4096-token causal prefill (config 4's per-sequence shape, 32/8 heads):
+    first 192 rows, rows across the middle and the last 64 rows checked in
+    full against the oracle."""
+    kvh, group, L = 8, 4, 4096
+    c, table, _, _, qh = _decode_case("bfloat16", 128, 16, kvh, group, [L], seed=4096)
+    blocks = table[0]
+    q = w.normal(77, L * qh * 128)
+    qd = torch.from_numpy(q).cuda()
+    out = torch.empty(L * qh * 128, device="cuda")
+    call(kv.lib.kvfx_attention, ctypes.byref(c.desc), qd.data_ptr(), out.data_ptr(), u64(blocks), L, L, qh,
+         None, 0, None)
+    got = out.cpu().numpy().reshape(L, -1)
+    for lo, hi in [(0, 192), (2000, 2056), (L - 64, L)]:
+        exp = oracle.attention_rows(c.host_k, c.host_v, 1, c.nb, kvh, 16, 128, blocks, L, L, qh, q, row_begin=lo,
+                                    row_end=hi, threads=16).reshape(L, -1)
+        err = float(np.abs(got[lo:hi] - exp[lo:hi]).max())
+        assert err < TOL["bfloat16"], (lo, err)
