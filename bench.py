@@ -54,6 +54,13 @@ def load_peak():
     return HBM_FALLBACK_GBS, "fallback"
 
 
+def load_bf16_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
 def traffic_ratio(kernel: str):
     """DRAM bytes per algorithmic byte from a committed ncu summary, if any."""
     p = ROOT / "profiles" / "ncu_traffic.json"
@@ -425,6 +432,67 @@ class WriteGather:
         return (time.perf_counter() - t) * 1e3 / steps, 2 * kh.numel() * 2 + len(slots) * 8
 
 
+class Prefill:
+    """Config 4 on one GPU: 8 sequences x 4096 tokens, 32 Q / 8 KV heads,
+    hd 128, bf16. Sequence 0 is written to 2056 tokens (128 full pages + a
+    partial page of 8), forked three times; each fork appends one token with a
+    copy-on-write of the shared partial page, then grows to 4096 with its own
+    K/V. Sequences 4-7 are independent. One step = the 8 causal prefill
+    attentions (query_tokens = kv_tokens = 4096)."""
+
+    def __init__(self, kv, w, cfg: dict):
+        import torch
+
+        self.kv = kv
+        L, H, G, hd, bs = cfg["tokens"], cfg["kv_heads"], cfg["q_heads"] // cfg["kv_heads"], cfg["head_size"], 16
+        self.L, self.qh, self.hd = L, H * G, hd
+        pages = cfg["sequences"] * (L // bs + 1) + 16
+        self.pool = kv.PhysicalBlockPool(pages, bs)
+        dev = torch.cuda.current_device()
+        self.storage = kv.PagedKVStorage(self.pool, H, hd, kv.DType.BFloat16, dev)
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(cfg["seed"])
+
+        def write(seq, lo, hi):
+            n = hi - lo
+            k = torch.randn(n * H * hd, generator=gen, device="cuda").to(torch.bfloat16)
+            v = torch.randn(n * H * hd, generator=gen, device="cuda").to(torch.bfloat16)
+            kv.write_paged_kv(self.storage, k, v, kv.build_slot_mapping([(seq, t) for t in range(lo, hi)]))
+
+        shared = cfg["shared_prefix"]
+        base = kv.SequenceState(0, self.pool)
+        base.append_tokens(shared)
+        write(base, 0, shared)
+        self.seqs = [base] + [base.fork_shared(i) for i in range(1, cfg["shared_group"])]
+        self.cow_copies = 0
+        for s in self.seqs[1:]:
+            loc = kv.append_token_cow(self.storage, s)  # byte-exact copy of the shared partial page
+            self.cow_copies += int(loc.offset_in_block != 0)
+            write(s, shared, shared + 1)
+        base.append_tokens(1)
+        write(base, shared, shared + 1)
+        for s in self.seqs:
+            s.append_tokens(L - shared - 1)
+            write(s, shared + 1, L)
+        for i in range(cfg["shared_group"], cfg["sequences"]):
+            s = kv.SequenceState(i, self.pool)
+            s.append_tokens(L)
+            write(s, 0, L)
+            self.seqs.append(s)
+        self.tables = [torch.from_numpy(np.array(kv.build_read_block_table(s), np.uint64).view(np.int64)).cuda()
+                       for s in self.seqs]
+        self.q = torch.randn(L * self.qh * hd, generator=gen, device="cuda")
+        self.o = torch.empty_like(self.q)
+        self.desc = kv.cache_descriptor(self.storage)
+        self.flops = len(self.seqs) * 2.0 * hd * L * (L + 1) * self.qh  # causal QK^T + PV
+
+    def launch(self, stream):
+        for t in self.tables:
+            rc = self.kv.lib.kvfx_attention(ctypes.byref(self.desc), self.q.data_ptr(), self.o.data_ptr(),
+                                            t.data_ptr(), self.L, self.L, self.qh, None, 0, stream)
+            self.kv.check(rc, "kvfx_attention")
+
+
 # ----------------------------------------------------------- CPU baseline ---
 
 def cpu_threads() -> int:
@@ -542,6 +610,13 @@ def only_case(args, ranks: Ranks, kv, w, peak: float) -> int:
         out = {"case": args.only, "batch": cfg["batch"], "ms_per_launch": ms, "kv_bytes": wl.kv_bytes,
                "algorithmic_bytes": wl.alg_bytes, "gbs": wl.alg_bytes / (ms * 1e-3) / 1e9,
                "pages_per_split": wl.pps}
+    elif args.only == "prefill4":
+        pf = Prefill(kv, w, w.CONFIG4)
+        per, total = time_launches(pf.launch, args.steps, args.warmup, ranks)
+        ms = total / args.steps
+        out = {"case": args.only, "ms_per_step": ms, "launches_per_step": len(pf.tables),
+               "tflops": pf.flops / (ms * 1e-3) / 1e12, "gbs": 0.0}
+        out["frac_of_bf16_peak"] = out["tflops"] / load_bf16_peak()[0]
     else:
         wg = WriteGather(kv, w, w.CONFIG2, ranks.rank, ranks.world)
         fn = wg.write if args.only == "write" else wg.gather
@@ -568,7 +643,7 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="headline decode only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather"],
+    ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather", "prefill4"],
                     help="run one kernel's case alone (profiling runs); prints a short JSON line")
     ap.add_argument("--batch", type=int, default=None, help="override the decode batch (profiling runs)")
     args = ap.parse_args(argv)
@@ -668,6 +743,20 @@ def main(argv=None) -> int:
             "kv_gbs": kv3 / (ms3 * 1e-3) / 1e9, "ms_per_step": ms3,
             "frac_of_peak": alg3 / (ms3 * 1e-3) / 1e9 / peak}
         del w3
+        torch.cuda.empty_cache()
+        if rank == 0:
+            pf = Prefill(kv, w, w.CONFIG4)
+            per4, tot4 = time_launches(pf.launch, 3, 3, Ranks(1))
+            ms4 = tot4 / 3
+            bf16_peak, bf16_kind = load_bf16_peak()
+            secondary["prefill_cfg4"] = {
+                "workload": "config4 causal prefill: 8 x 4096 tokens, 32Q/8KV hd128 bf16, sequences 0-3 share 2056 "
+                            "tokens (partial page copy-on-written), tcgen05 kernel",
+                "ms_per_step": ms4, "launches_per_step": len(pf.tables), "cow_page_copies": pf.cow_copies,
+                "algorithmic_tflops": pf.flops / (ms4 * 1e-3) / 1e12,
+                "frac_of_bf16_peak": pf.flops / (ms4 * 1e-3) / 1e12 / bf16_peak, "peak_kind": bf16_kind,
+                "tensor_flops_executed_per_algorithmic": 2.0}
+            del pf
 
     clocks = clk.summary()
     if rank == 0:
