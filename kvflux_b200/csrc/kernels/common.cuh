@@ -87,6 +87,30 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, unsigne
     }
 }
 
+// Slow part of mbar_wait_lean, kept out of line so that each call site adds
+// only one try_wait to the caller's code (for kernels whose hot loops must
+// stay small in the instruction cache).
+static __device__ __noinline__ bool mbar_wait_slow(uint32_t a, uint32_t phase, unsigned* status) {
+    const uint64_t start = globaltimer_ns();
+    for (uint32_t spin = 0;; ++spin) {
+        if (mbar_try_wait(a, phase)) return true;
+        if ((spin & 15u) == 15u) {
+            if (globaltimer_ns() - start > kWaitLimitNs) {
+                raise_flag(status, KVFX_FLAG_TIMEOUT);
+                return false;
+            }
+            __nanosleep(32);
+        }
+    }
+}
+
+// Same contract as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_lean(uint64_t* bar, uint32_t phase, unsigned* status) {
+    const uint32_t a = smem_addr(bar);
+    if (mbar_try_wait(a, phase)) return true;
+    return mbar_wait_slow(a, phase, status);
+}
+
 // ---------------------------------------------------------- bulk copies ---
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes % 16 == 0,
@@ -133,6 +157,19 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Per-thread register budget of the executing warpgroup (all 128 threads
+// execute it together). The increases of all warpgroups must fit in what
+// the block was launched with (threads x registers per thread), or an
+// increase waits for registers that are never released.
+template <uint32_t N>
+__device__ __forceinline__ void regs_increase() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_decrease() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ------------------------------------------------------------ tensor ops ---
@@ -192,6 +229,58 @@ template <> struct Elem<__nv_bfloat16> {
         return *reinterpret_cast<uint32_t*>(&h);
     }
 };
+
+// 2^x by the MUFU approximation (flush-to-zero; 2^-inf = +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// max(a, b, c) in one instruction (sm_100 three-input form).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// Two floats in one 64-bit register pair, for the sm_100 packed f32x2 ops.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t x, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x));
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t x, uint64_t y) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t x, uint64_t y) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+    return r;
+}
+
+// Same split as split2 below with one rounding per pair: the packed hi is
+// widened back by bit moves (bf16) or conversions (fp16) instead of a
+// second round of the already representable values.
+template <typename T>
+__device__ __forceinline__ void split2_fast(float x0, float x1, uint32_t& hi, uint32_t& lo);
+template <>
+__device__ __forceinline__ void split2_fast<__nv_bfloat16>(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    hi = Elem<__nv_bfloat16>::pack(x0, x1);
+    const float h0 = __uint_as_float(hi << 16), h1 = __uint_as_float(hi & 0xFFFF0000u);
+    lo = Elem<__nv_bfloat16>::pack(x0 - h0, x1 - h1);
+}
+template <>
+__device__ __forceinline__ void split2_fast<__half>(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    hi = Elem<__half>::pack(x0, x1);
+    const __half2 h = *reinterpret_cast<const __half2*>(&hi);
+    lo = Elem<__half>::pack(x0 - __low2float(h), x1 - __high2float(h));
+}
 
 // Splits x into hi + lo, both representable in T, with hi = round(x) and
 // lo = round(x - hi); hi + lo carries about twice T's mantissa bits.

@@ -1,25 +1,37 @@
 // Causal prefill PagedAttention on the 5th-generation tensor cores (kernel 4).
 //
-// One CTA = 128 query rows (a query tile) of one Q head of one sequence,
-// against the KV tiles of 64 tokens (4 pages) that the tile's rows can see.
-// Warp roles:
-//   warp 0      TMA producer: per KV tile, 16 tensor loads (4 pages x 2
-//               64-dim halves, K and V; 128-byte swizzle, no multicast) into a
-//               3-stage ring.
-//   warp 1      owns TMEM (256 columns: S0, S1, O) and issues every tcgen05.mma
-//               from one thread: S_j = Q K_j^T into S[j%2] while the softmax
-//               works on S[(j-1)%2], then O += P_{j-1} V_{j-1}.
-//   warps 2..5  softmax, one query row per thread (TMEM lane = row): scores
-//               from TMEM, causal mask, online softmax in base 2, P to shared
-//               memory; at the end O / l from TMEM to global memory.
-// Precision: Q (FP32 in the API) and P are each fed as two bf16/fp16
-// operands, hi = round(x) and lo = round(x - hi), accumulated into the same
-// TMEM tile (S = Q_hi K + Q_lo K, O += P_hi V + P_lo V), which keeps ~16
-// mantissa bits and FP32-class error against the FP64 reference; rounding Q
-// or P to 16 bits alone exceeds 2e-3 at 4096 tokens.
-// O is rescaled in TMEM only when a tile's row maximum exceeds the running
-// one by more than 8 (base-2 units). Tokens past the sequence end in the last
-// tile are masked in S and zeroed in the V tile.
+// Persistent: one CTA per SM walks a list of work units, one unit = a query
+// tile of 128 rows of one Q head against the KV tiles of 128 tokens (8 pages)
+// that its rows can see. Units are ordered heaviest first (last query tiles
+// first) and dealt to CTAs in snake order (round r: CTA c takes unit
+// r*G + c, or r*G + G-1-c on odd rounds), which evens out the causal
+// triangle's unequal work. Tiles of consecutive units form one stream per
+// CTA, so loads, MMAs and softmax run across unit boundaries without a drain.
+// Warp roles (12 warps):
+//   warp 0      K producer, warp 2 V producer: per KV tile 16 tensor loads
+//               (8 pages x 2 64-dim halves, 128-byte swizzle, no multicast)
+//               into a 3-slot K ring and a 2-slot V ring.
+//   warp 1      owns TMEM (512 columns) and issues every tcgen05.mma from one
+//               thread: S(g) = Q K_g^T into S[g%3], then O += P(g) V_g with
+//               P read from TMEM; QK runs two tiles ahead of PV.
+//   warp 3      idle.
+//   warps 4-7   softmax, one query row per thread (TMEM lane = row): scores
+//               from TMEM, causal mask, online softmax in base 2, P = exp2(S-m)
+//               written back over its own S columns as packed 16-bit hi/lo
+//               pairs; at a unit's last tile, O / l from TMEM to global memory.
+//   warps 8-11  Q staging: the next unit's Q rows are loaded into registers
+//               while the current unit runs, and split into hi/lo 16-bit
+//               halves in shared memory once its last QK has completed.
+// TMEM columns: S/P buffers 0, 128, 256; O 384. S[b] holds P(g) (g%3 == b)
+// until PV(g) completes; the MMA thread waits for that completion before
+// writing S(g+3) there, while PV(g+1) keeps the tensor pipe busy.
+// Precision: Q (FP32 in the API) and P are each fed as two 16-bit operands,
+// hi = round(x) and lo = round(x - hi), accumulated into the same TMEM tile
+// (S = Q_hi K + Q_lo K, O += P_hi V + P_lo V): ~16 mantissa bits and FP32-class
+// error against the FP64 reference; rounding Q or P to 16 bits alone exceeds
+// 2e-3 at 4096 tokens. O is rescaled in TMEM only when a tile's row maximum
+// exceeds the running one by more than 8 (base-2 units). Tokens past the
+// sequence end in the last tile are masked in S and zeroed in the V tile.
 //
 // Semantics: KVFlux src/v2/paged_attention.cu:109-128 (query i sees
 // positions <= kv_tokens - query_tokens + i; KV head = q_head / group).
@@ -33,36 +45,90 @@
 namespace kvfx {
 namespace {
 
-constexpr int kBM = 128;        // query rows per CTA
-constexpr int kBN = 64;         // KV tokens per tile (4 pages of 16)
-constexpr int kHD = 128;        // head size handled here
-constexpr int kStages = 3;      // K/V ring depth
-constexpr int kThreads = 192;   // 6 warps
-constexpr uint32_t kTmemCols = 256;
+constexpr int kBM = 128;         // query rows per unit
+constexpr int kBN = 128;         // KV tokens per tile (8 pages of 16)
+constexpr int kHD = 128;         // head size handled here
+constexpr int kKStages = 3;      // K ring depth
+constexpr int kVStages = 2;      // V ring depth
+constexpr int kSBufs = 3;        // S/P buffers in TMEM
+constexpr int kThreads = 384;    // 12 warps
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemO = kSBufs * kBN;          // O accumulator column
 
 // Shared-memory layout (byte offsets from a 1024-aligned base).
-constexpr uint32_t kQAtom = kBM * 128;            // [128 rows][64 dims] 16-bit, 16 KiB
-constexpr uint32_t kQBytes = 2 * kQAtom;          // 128 dims
-constexpr uint32_t kKVHalf = kBN * 128;           // [64 tokens][64 dims], 8 KiB
-constexpr uint32_t kKVTile = 2 * kKVHalf;         // 16 KiB
-constexpr uint32_t kOffQHi = 0;
-constexpr uint32_t kOffQLo = kOffQHi + kQBytes;
-constexpr uint32_t kOffK = kOffQLo + kQBytes;
-constexpr uint32_t kOffV = kOffK + kStages * kKVTile;
-constexpr uint32_t kOffPHi = kOffV + kStages * kKVTile;
-constexpr uint32_t kOffPLo = kOffPHi + kBM * 128;
-constexpr uint32_t kSmemBytes = kOffPLo + kBM * 128;   // 192 KiB
+constexpr uint32_t kQAtom = kBM * 128;             // [128 rows][64 dims] 16-bit, 16 KiB
+constexpr uint32_t kQBytes = 2 * kQAtom;           // 128 dims, 32 KiB (hi; lo follows)
+constexpr uint32_t kKVHalf = kBN * 128;            // [128 tokens][64 dims], 16 KiB
+constexpr uint32_t kKVTile = 2 * kKVHalf;          // 32 KiB
+constexpr uint32_t kOffQ = 0;
+constexpr uint32_t kOffK = kOffQ + 2 * kQBytes;
+constexpr uint32_t kOffV = kOffK + kKStages * kKVTile;
+constexpr uint32_t kSmemBytes = kOffV + kVStages * kKVTile;   // 224 KiB
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
 
 struct PrefillParams {
     const float* q;
     float* o;
     const uint64_t* blocks;
-    uint64_t q_tokens, kv_tokens, num_blocks;
+    uint64_t q_tokens, kv_tokens, num_blocks, n_units;
     uint32_t q_heads, kv_heads, group, n_qtiles;
     float qscale;
     unsigned* status;
 };
+
+struct Unit {
+    uint64_t q0;
+    uint32_t qh, kh, ntiles;
+};
+
+// The unit this CTA takes in round `round` (false when it has none left).
+__device__ __forceinline__ bool unit_at(const PrefillParams& p, uint32_t round, Unit& u) {
+    const uint64_t G = gridDim.x;
+    const uint64_t base = static_cast<uint64_t>(round) * G;
+    if (base >= p.n_units) return false;
+    const uint64_t idx = base + ((round & 1u) ? (G - 1 - blockIdx.x) : blockIdx.x);
+    if (idx >= p.n_units) return false;  // partial last round
+    const uint32_t qtile = p.n_qtiles - 1 - static_cast<uint32_t>(idx / p.q_heads);
+    u.qh = static_cast<uint32_t>(idx % p.q_heads);
+    u.kh = u.qh / p.group;
+    u.q0 = static_cast<uint64_t>(qtile) * kBM;
+    const uint64_t q_last = umin64(u.q0 + kBM, p.q_tokens) - 1;
+    u.ntiles = static_cast<uint32_t>((p.kv_tokens - p.q_tokens + q_last) / kBN + 1);
+    return true;
+}
+
+// Position in this CTA's stream of KV tiles: unit ordinal k, tile j of the
+// unit, and the running tile ordinal g that indexes rings and barriers.
+struct TileCursor {
+    Unit u;
+    uint32_t round, k, j, g;
+    bool valid;
+    __device__ __forceinline__ void init(const PrefillParams& p) {
+        round = k = j = g = 0;
+        valid = unit_at(p, 0, u);
+    }
+    __device__ __forceinline__ void next(const PrefillParams& p) {
+        ++g;
+        if (++j < u.ntiles) return;
+        j = 0;
+        ++k;
+        valid = unit_at(p, ++round, u);
+    }
+    __device__ __forceinline__ bool last() const { return j + 1 == u.ntiles; }
+};
+
+// The two 16-bit values of a packed pair, widened to float (low half first).
+template <typename T>
+__device__ __forceinline__ uint64_t widen2(uint32_t h);
+template <>
+__device__ __forceinline__ uint64_t widen2<__nv_bfloat16>(uint32_t h) {
+    return f2_pack(__uint_as_float(h << 16), __uint_as_float(h & 0xFFFF0000u));
+}
+template <>
+__device__ __forceinline__ uint64_t widen2<__half>(uint32_t h) {
+    const __half2 x = *reinterpret_cast<const __half2*>(&h);
+    return f2_pack(__low2float(x), __high2float(x));
+}
 
 // Byte offset of 16-byte chunk `c` of row `r` in a K-major 128-byte-swizzled
 // atom of rows 128 bytes wide.
@@ -70,45 +136,79 @@ __device__ __forceinline__ uint32_t swz_row(uint32_t r, uint32_t c) {
     return (r >> 3) * 1024 + (r & 7) * 128 + (((c ^ r) & 7) << 4);
 }
 
+// One KV tile (8 pages of one KV head) into a ring slot.
+__device__ __forceinline__ void load_kv_tile(const PrefillParams& p, const CUtensorMap* map, unsigned char* dst,
+                                             uint32_t kh, uint32_t j, uint64_t npages, uint64_t* bar) {
+    mbar_arrive_expect_tx(bar, kKVTile);
+#pragma unroll 2
+    for (int pg = 0; pg < kBN / 16; ++pg) {
+        const uint64_t lp = static_cast<uint64_t>(j) * (kBN / 16) + pg;
+        uint64_t blk = __ldg(p.blocks + (lp < npages ? lp : 0));
+        if (blk >= p.num_blocks) {
+            raise_flag(p.status, KVFX_FLAG_BAD_INDEX);
+            blk = 0;
+        }
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+            tma_load_4d(dst + b * kKVHalf + pg * 2048, map, b * 64, 0, static_cast<int>(kh), static_cast<int>(blk),
+                        bar);
+        }
+    }
+}
+
+// Producer loop of one ring (K or V): waits for the slot's previous tile to be
+// consumed, loads the next, then waits for its own copies in flight.
+__device__ __noinline__ void produce(const PrefillParams& p, const CUtensorMap* map, unsigned char* ring,
+                                     uint64_t* full, uint64_t* empty, uint64_t npages, uint32_t kStages) {
+    prefetch_tensormap(map);
+    TileCursor c;
+    c.init(p);
+    uint32_t issued = 0;
+    for (; c.valid; c.next(p)) {
+        const uint32_t g = c.g, st = g % kStages;
+        if (g >= kStages && !mbar_wait_lean(&empty[st], ((g / kStages) - 1) & 1u, p.status)) break;
+        load_kv_tile(p, map, ring + st * kKVTile, c.u.kh, c.j, npages, &full[st]);
+        issued = g + 1;
+    }
+    for (uint32_t g = issued > kStages ? issued - kStages : 0; g < issued; ++g)
+        (void)mbar_wait_lean(&full[g % kStages], (g / kStages) & 1u, p.status);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
 prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap) {
     extern __shared__ unsigned char smem_raw[];
-    __shared__ uint64_t kv_full[kStages], kv_empty[kStages];
-    __shared__ uint64_t s_full[2], s_empty[2];
-    __shared__ uint64_t q_full, p_full, o_done, mma_done;
+    __shared__ uint64_t k_full[kKStages], k_empty[kKStages], v_full[kVStages], v_empty[kVStages];
+    __shared__ uint64_t s_full[kSBufs], p_full[kSBufs], pv_done[kSBufs];
+    __shared__ uint64_t q_full, q_free, o_full, o_free, mma_done;
     __shared__ uint32_t tmem_base_slot;
-    __shared__ int abort_flag;
 
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_addr(smem);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-    const uint32_t qtile = p.n_qtiles - 1 - blockIdx.x;  // heaviest tiles first
-    const uint32_t qh = blockIdx.y;
-    const uint32_t kh = qh / p.group;
-    const uint64_t q0 = static_cast<uint64_t>(qtile) * kBM;
-    const uint64_t q_last = umin64(q0 + kBM, p.q_tokens) - 1;
-    const uint64_t last_pos = p.kv_tokens - p.q_tokens + q_last;
-    const uint32_t ntiles = static_cast<uint32_t>(last_pos / kBN + 1);
     const uint64_t npages = ceil_div(p.kv_tokens, 16);
 
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+        for (int s = 0; s < kKStages; ++s) {
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
         }
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(&s_full[s], 1);
-            mbar_init(&s_empty[s], 128);
+        for (int s = 0; s < kVStages; ++s) {
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
+        }
+        for (int b = 0; b < kSBufs; ++b) {
+            mbar_init(&s_full[b], 1);
+            mbar_init(&p_full[b], 128);
+            mbar_init(&pv_done[b], 1);
         }
         mbar_init(&q_full, 128);
-        mbar_init(&p_full, 128);
-        mbar_init(&o_done, 1);
+        mbar_init(&q_free, 1);
+        mbar_init(&o_full, 1);
+        mbar_init(&o_free, 128);
         mbar_init(&mma_done, 1);
-        abort_flag = 0;
         fence_mbarrier_init();
     }
     if (warp == 1) {
@@ -119,237 +219,257 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = tmem_base_slot;
-    const uint32_t tS[2] = {tmem, tmem + kBN};
-    const uint32_t tO = tmem + 2 * kBN;
 
     if (warp == 0) {
-        // ------------------------------------------------------ producer ---
-        if (lane == 0) {
-            prefetch_tensormap(&kmap);
-            prefetch_tensormap(&vmap);
-            for (uint32_t j = 0; j < ntiles; ++j) {
-                const int st = static_cast<int>(j % kStages);
-                if (j >= kStages && !mbar_wait(&kv_empty[st], ((j - kStages) / kStages) & 1u, p.status)) {
-                    abort_flag = 1;
-                    break;
-                }
-                mbar_arrive_expect_tx(&kv_full[st], 2 * kKVTile);
-                unsigned char* kt = smem + kOffK + st * kKVTile;
-                unsigned char* vt = smem + kOffV + st * kKVTile;
-#pragma unroll
-                for (int pg = 0; pg < kBN / 16; ++pg) {
-                    const uint64_t lp = static_cast<uint64_t>(j) * (kBN / 16) + pg;
-                    uint64_t blk = __ldg(p.blocks + (lp < npages ? lp : 0));
-                    if (blk >= p.num_blocks) {
-                        raise_flag(p.status, KVFX_FLAG_BAD_INDEX);
-                        blk = 0;
-                    }
-#pragma unroll
-                    for (int b = 0; b < 2; ++b) {
-                        tma_load_4d(kt + b * kKVHalf + pg * 2048, &kmap, b * 64, 0, static_cast<int>(kh),
-                                    static_cast<int>(blk), &kv_full[st]);
-                        tma_load_4d(vt + b * kKVHalf + pg * 2048, &vmap, b * 64, 0, static_cast<int>(kh),
-                                    static_cast<int>(blk), &kv_full[st]);
-                    }
-                }
-            }
-        }
+        // ---------------------------------------------------- K producer ---
+        if (lane == 0) produce(p, &kmap, smem + kOffK, k_full, k_empty, npages, kKStages);
+    } else if (warp == 2) {
+        // ---------------------------------------------------- V producer ---
+        if (lane == 0) produce(p, &vmap, smem + kOffV, v_full, v_empty, npages, kVStages);
     } else if (warp == 1) {
         // ----------------------------------------------------- MMA issuer ---
         if (lane == 0) {
-            constexpr bool kBF = sizeof(T) == 2 && !std::is_same<T, __half>::value;
+            constexpr bool kBF = std::is_same<T, __nv_bfloat16>::value;
             const uint32_t id_qk = tc::idesc_f16(kBM, kBN, kBF, false);
             const uint32_t id_pv = tc::idesc_f16(kBM, kHD, kBF, true);
-            bool ok = mbar_wait(&q_full, 0, p.status);
-            auto issue_pv = [&](uint32_t jj) {
-                const uint32_t vt = sbase + kOffV + (jj % kStages) * kKVTile;
-#pragma unroll
-                for (int part = 0; part < 2; ++part) {  // P_hi then P_lo
-                    const uint32_t pa = sbase + (part == 0 ? kOffPHi : kOffPLo);
-#pragma unroll
-                    for (int t = 0; t < kBN / 16; ++t) {
-                        tc::mma(tO, tc::desc_k_major(pa + t * 32), tc::desc_mn_major(vt + t * 2048, kKVHalf), id_pv,
-                                (jj > 0 || part > 0 || t > 0) ? 1u : 0u);
-                    }
-                }
-                tc::commit(&o_done);
-                tc::commit(&kv_empty[jj % kStages]);
-            };
-            for (uint32_t j = 0; ok && j < ntiles; ++j) {
-                const int st = static_cast<int>(j % kStages);
-                if (!mbar_wait(&kv_full[st], (j / kStages) & 1u, p.status)) {
-                    ok = false;
-                    break;
-                }
-                if (j >= 2 && !mbar_wait(&s_empty[j & 1], ((j - 2) / 2) & 1u, p.status)) {
-                    ok = false;
-                    break;
-                }
+            // Operand descriptors are formed once; every MMA adds a constant
+            // offset (16-byte units, the descriptor's low start-address field;
+            // shared addresses stay below 2^18 so nothing carries out).
+            const uint64_t q_desc0 = tc::desc_k_major(sbase + kOffQ);
+            const uint64_t k_desc0 = tc::desc_k_major(sbase + kOffK);
+            const uint64_t v_desc0 = tc::desc_mn_major(sbase + kOffV, kKVHalf);
+            TileCursor qk, pv;
+            qk.init(p);
+            pv.init(p);
+            // S(g) = Q K_g^T into S[g%3]; S[g%3] held P(g-3) until PV(g-3) completed.
+            auto issue_qk = [&]() -> bool {
+                const uint32_t g = qk.g, b = g % kSBufs, st = g % kKStages;
+                if (qk.j == 0 && !mbar_wait_lean(&q_full, qk.k & 1u, p.status)) return false;
+                if (!mbar_wait_lean(&k_full[st], (g / kKStages) & 1u, p.status)) return false;
+                if (g >= kSBufs && !mbar_wait_lean(&pv_done[b], ((g / kSBufs) - 1) & 1u, p.status)) return false;
                 tc::fence_after_sync();
-                const uint32_t kt = sbase + kOffK + st * kKVTile;
+                const uint32_t d = tmem + b * kBN;
+                const uint64_t k_desc = k_desc0 + ((st * kKVTile) >> 4);
+                // 16 MMAs: Q_hi then Q_lo, 8 K-steps of 16 each (unrolled: the
+                // constant operand offsets fold into the descriptor adds).
 #pragma unroll
-                for (int part = 0; part < 2; ++part) {  // Q_hi then Q_lo
-                    const uint32_t qa = sbase + (part == 0 ? kOffQHi : kOffQLo);
+                for (uint32_t i = 0; i < 16; ++i) {
+                    const uint32_t part = i >> 3, kk = i & 7;
+                    const uint32_t a_off = part * kQBytes + (kk >> 2) * kQAtom + (kk & 3) * 32;
+                    const uint32_t b_off = (kk >> 2) * kKVHalf + (kk & 3) * 32;
+                    tc::mma(d, q_desc0 + (a_off >> 4), k_desc + (b_off >> 4), id_qk, i > 0 ? 1u : 0u);
+                }
+                tc::commit(&s_full[b]);
+                tc::commit(&k_empty[st]);
+                if (qk.last()) tc::commit(&q_free);  // Q may be replaced once this completes
+                qk.next(p);
+                return true;
+            };
+            // O += P(g) V_g with P from TMEM; a unit's first PV overwrites O,
+            // which the previous unit's epilogue must have read.
+            auto issue_pv = [&]() -> bool {
+                const uint32_t g = pv.g, b = g % kSBufs, sv = g % kVStages;
+                if (pv.j == 0 && pv.k >= 1 && !mbar_wait_lean(&o_free, (pv.k - 1) & 1u, p.status)) return false;
+                if (!mbar_wait_lean(&v_full[sv], (g / kVStages) & 1u, p.status)) return false;
+                if (!mbar_wait_lean(&p_full[b], (g / kSBufs) & 1u, p.status)) return false;
+                tc::fence_after_sync();
+                const uint32_t pt = tmem + b * kBN;
+                const uint64_t v_desc = v_desc0 + ((sv * kKVTile) >> 4);
+                // 16 MMAs: 8 K-steps of 16 tokens, P_hi then P_lo for each.
 #pragma unroll
-                    for (int kk = 0; kk < kHD / 16; ++kk) {
-                        const uint32_t a = qa + (kk >> 2) * kQAtom + (kk & 3) * 32;
-                        const uint32_t b = kt + (kk >> 2) * kKVHalf + (kk & 3) * 32;
-                        tc::mma(tS[j & 1], tc::desc_k_major(a), tc::desc_k_major(b), id_qk,
-                                (part > 0 || kk > 0) ? 1u : 0u);
-                    }
+                for (uint32_t i = 0; i < 16; ++i) {
+                    const uint32_t t = i >> 1, part = i & 1;
+                    const uint32_t a = pt + (t >> 1) * 32 + part * 16 + (t & 1) * 8;
+                    tc::mma_ts(tmem + kTmemO, a, v_desc + ((t * 2048) >> 4), id_pv, (pv.j > 0 || i > 0) ? 1u : 0u);
                 }
-                tc::commit(&s_full[j & 1]);
-                if (j >= 1) {
-                    if (!mbar_wait(&p_full, (j - 1) & 1u, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    tc::fence_after_sync();
-                    issue_pv(j - 1);
-                }
+                tc::commit(&pv_done[b]);
+                tc::commit(&v_empty[sv]);
+                if (pv.last()) tc::commit(&o_full);
+                pv.next(p);
+                return true;
+            };
+            bool ok = true;
+            for (int i = 0; i < 2 && ok && qk.valid; ++i) ok = issue_qk();
+            while (ok && pv.valid) {
+                ok = issue_pv();
+                if (ok && qk.valid) ok = issue_qk();
             }
-            if (ok && ntiles > 0) {
-                if (mbar_wait(&p_full, (ntiles - 1) & 1u, p.status)) {
-                    tc::fence_after_sync();
-                    issue_pv(ntiles - 1);
-                } else {
-                    ok = false;
-                }
-            }
-            if (!ok) abort_flag = 1;
             // Every MMA this thread issued is complete before TMEM is released.
             tc::commit(&mma_done);
-            (void)mbar_wait(&mma_done, 0, p.status);
+            (void)mbar_wait_lean(&mma_done, 0, p.status);
         }
-    } else {
+    } else if (warp >= 4 && warp < 8) {
         // -------------------------------------------------------- softmax ---
         const uint32_t quarter = static_cast<uint32_t>(warp & 3);  // TMEM lanes this warp may access
-        const uint32_t r = quarter * 32 + lane;                     // query row within the tile
-        const uint64_t qi = q0 + r;
-        const bool row_live = qi < p.q_tokens;
-        const uint64_t pos = p.kv_tokens - p.q_tokens + qi;         // last visible position
+        const uint32_t r = quarter * 32 + lane;                     // query row within the unit
         const uint32_t lane_base = (quarter * 32) << 16;
-
-        // Q row -> scaled hi/lo 16-bit halves in the swizzled K-major tiles.
-        {
-            const float* qrow = p.q + (qi * p.q_heads + qh) * kHD;
-            unsigned char* qhi = smem + kOffQHi;
-            unsigned char* qlo = smem + kOffQLo;
-#pragma unroll 4
-            for (uint32_t c = 0; c < kHD / 8; ++c) {
-                float x[8];
-                if (row_live) {
-                    const float4 a = *reinterpret_cast<const float4*>(qrow + c * 8);
-                    const float4 b = *reinterpret_cast<const float4*>(qrow + c * 8 + 4);
-                    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-                    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) x[e] = 0.f;
-                }
-                uint32_t hi[4], lo[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) split2<T>(x[2 * e] * p.qscale, x[2 * e + 1] * p.qscale, hi[e], lo[e]);
-                const uint32_t off = (c >> 3) * kQAtom + swz_row(r, c & 7);
-                *reinterpret_cast<uint4*>(qhi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4*>(qlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-            }
-            fence_proxy_async_smem();
-            mbar_arrive(&q_full);
-        }
-
+        const uint32_t tO = tmem + kTmemO + lane_base;
         // tcgen05.ld/st are warp-collective: every wait result is made
         // warp-uniform so that no lane skips one the others execute.
         auto wait_all = [&](uint64_t* bar, uint32_t phase) {
-            return __all_sync(0xffffffffu, mbar_wait(bar, phase, p.status)) != 0;
+            return __all_sync(0xffffffffu, mbar_wait_lean(bar, phase, p.status)) != 0;
         };
-        float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
-        for (uint32_t j = 0; j < ntiles; ++j) {
-            if (!wait_all(&s_full[j & 1], (j / 2) & 1u)) {
-                ok = false;
-                break;
-            }
-            tc::fence_after_sync();
-            float s[kBN];
-            tc::ld32(tS[j & 1] + lane_base, s);
-            tc::ld32(tS[j & 1] + lane_base + 32, s + 32);
-            tc::wait_ld();
-            tc::fence_before_sync();
-            mbar_arrive(&s_empty[j & 1]);
-
-            const uint64_t t0 = static_cast<uint64_t>(j) * kBN;
-            float mx = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < kBN; ++c) {
-                const uint64_t t = t0 + c;
-                s[c] = (t <= pos && t < p.kv_tokens) ? s[c] : -INFINITY;
-                mx = fmaxf(mx, s[c]);
-            }
-            // P's buffer (and O) are free once the previous tile's PV is done.
-            if (j >= 1 && !wait_all(&o_done, (j - 1) & 1u)) {
-                ok = false;
-                break;
-            }
-            const bool need = mx > m_run + 8.f;  // m_run = -inf: always at tile 0
-            const float m_new = need ? mx : m_run;
-            const float alpha = exp2f(m_run - m_new);  // 1 if unchanged, 0 at the first tile
-            if (j >= 1 && __any_sync(0xffffffffu, need)) {
+        uint32_t g = 0;  // running tile ordinal, as in the MMA thread
+        Unit u;
+        for (uint32_t round = 0, k = 0; ok && unit_at(p, round, u); ++round, ++k) {
+            // Last visible position of this row.
+            const int64_t pos = static_cast<int64_t>(p.kv_tokens - p.q_tokens + u.q0 + r);
+            float m_run = -INFINITY, l_run = 0.f;
+            for (uint32_t j = 0; j < u.ntiles; ++j, ++g) {
+                const uint32_t b = g % kSBufs;
+                if (!wait_all(&s_full[b], (g / kSBufs) & 1u)) { ok = false; break; }
                 tc::fence_after_sync();
-#pragma unroll 1
-                for (int cb = 0; cb < kHD; cb += 32) {
-                    float ov[32];
-                    tc::ld32(tO + lane_base + cb, ov);
-                    tc::wait_ld();
+                const uint32_t tS = tmem + b * kBN + lane_base;
+                // Causal mask: column c is visible iff j*128 + c <= pos (pos <
+                // kv_tokens for live rows). Applied branch-free as
+                // min(s, +-inf), so that NaN scores of masked columns become
+                // -inf as well; only tiles on or past the diagonal need it.
+                const int64_t lim64 = pos - static_cast<int64_t>(j) * kBN;
+                const int lim = lim64 < -1 ? -1 : (lim64 > kBN ? kBN : static_cast<int>(lim64));
+                const bool masked = !__all_sync(0xffffffffu, lim >= kBN - 1);
+                auto mask32 = [&](float* v, int rel) {  // rel: lim relative to v[0]
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) ov[e] *= alpha;
-                    tc::st32(tO + lane_base + cb, ov);
+                    for (int cc = 0; cc < 32; ++cc, --rel)
+                        v[cc] = fminf(v[cc], __uint_as_float(0x7F800000u | (static_cast<uint32_t>(rel) & 0x80000000u)));
+                };
+                auto max32 = [](const float* v) {
+                    float m[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) m[e] = fmax3(v[e], v[4 + e], v[8 + e]);
+#pragma unroll
+                    for (int q = 12; q < 28; q += 8) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) m[e] = fmax3(m[e], v[q + e], v[q + 4 + e]);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) m[e] = fmaxf(m[e], v[28 + e]);
+                    return fmaxf(fmax3(m[0], m[1], m[2]), m[3]);
+                };
+                // Row maximum: all 128 scores in one TMEM round trip, or chunk
+                // by chunk with the mask on diagonal tiles.
+                float mx = -INFINITY;
+                if (!masked) {
+                    float sc[kBN];
+#pragma unroll
+                    for (int cb = 0; cb < kBN; cb += 32) tc::ld32(tS + cb, sc + cb);
+                    tc::wait_ld32(sc);
+                    tc::reg_fence32(sc + 32);
+                    tc::reg_fence32(sc + 64);
+                    tc::reg_fence32(sc + 96);
+                    mx = fmaxf(fmaxf(max32(sc), max32(sc + 32)), fmaxf(max32(sc + 64), max32(sc + 96)));
+                } else {
+#pragma unroll 1
+                    for (int cb = 0; cb < kBN; cb += 32) {
+                        float sc[32];
+                        tc::ld32(tS + cb, sc);
+                        tc::wait_ld32(sc);
+                        mask32(sc, lim - cb);
+                        mx = fmaxf(mx, max32(sc));
+                    }
+                }
+                const bool need = mx > m_run + 8.f;  // m_run = -inf: always at a unit's first tile
+                const float m_new = need ? mx : m_run;
+                const float alpha = ex2_approx(m_run - m_new);  // 1 if unchanged, 0 at the first tile
+                if (j >= 1 && __any_sync(0xffffffffu, need)) {
+                    // O holds P(0..j-1) V once PV(g-1) completes; PV(g) is
+                    // not issued before this tile's P is published.
+                    if (!wait_all(&pv_done[(g - 1) % kSBufs], ((g - 1) / kSBufs) & 1u)) { ok = false; break; }
+                    tc::fence_after_sync();
+#pragma unroll 1
+                    for (int cb = 0; cb < kHD; cb += 32) {
+                        float ov[32];
+                        tc::ld32(tO + cb, ov);
+                        tc::wait_ld32(ov);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) ov[e] *= alpha;
+                        tc::st32(tO + cb, ov);
+                    }
+                }
+                m_run = m_new;
+                // P = exp2(S - m) as packed hi/lo pairs over the tile's own S
+                // columns: chunk c (tokens 32c..32c+31) -> hi at 32c, lo at
+                // 32c + 16. The scores are read again from TMEM chunk by
+                // chunk, the next chunk's load overlapping this chunk's math.
+                const uint64_t mm = f2_pack(m_run, m_run);
+                uint64_t lsum0 = f2_pack(0.f, 0.f), lsum1 = lsum0;
+                auto p_chunk = [&](int c, float* v) {
+                    if (masked) mask32(v, lim - 32 * c);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t hi[8], lo[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            float x0, x1;
+                            f2_unpack(f2_sub(f2_pack(v[16 * h + 2 * e], v[16 * h + 2 * e + 1]), mm), x0, x1);
+                            x0 = ex2_approx(x0);
+                            x1 = ex2_approx(x1);
+                            const uint64_t pe = f2_pack(x0, x1);
+                            if (e & 1) lsum1 = f2_add(lsum1, pe);
+                            else lsum0 = f2_add(lsum0, pe);
+                            hi[e] = Elem<T>::pack(x0, x1);
+                            float r0, r1;
+                            f2_unpack(f2_sub(pe, widen2<T>(hi[e])), r0, r1);
+                            lo[e] = Elem<T>::pack(r0, r1);
+                        }
+                        tc::st8(tS + 32 * c + 8 * h, hi);
+                        tc::st8(tS + 32 * c + 16 + 8 * h, lo);
+                    }
+                };
+                {
+                    float va[32], vb[32];
+                    tc::ld32(tS, va);
+                    tc::wait_ld32(va);
+#pragma unroll 1
+                    for (int c = 0; c < kBN / 32; c += 2) {
+                        tc::ld32(tS + 32 * (c + 1), vb);
+                        p_chunk(c, va);
+                        tc::wait_ld32(vb);
+                        if (c + 2 < kBN / 32) tc::ld32(tS + 32 * (c + 2), va);
+                        p_chunk(c + 1, vb);
+                        if (c + 2 < kBN / 32) tc::wait_ld32(va);
+                    }
+                }
+                {
+                    float s0, s1, s2, s3;
+                    f2_unpack(lsum0, s0, s1);
+                    f2_unpack(lsum1, s2, s3);
+                    l_run = l_run * alpha + ((s0 + s1) + (s2 + s3));
                 }
                 tc::wait_st();
-            }
-            l_run *= alpha;
-            m_run = m_new;
-            // P = exp2(S - m) as hi/lo halves in the swizzled K-major P tiles.
-            unsigned char* phi = smem + kOffPHi;
-            unsigned char* plo = smem + kOffPLo;
-#pragma unroll
-            for (int c = 0; c < kBN / 8; ++c) {
-                uint32_t hi[4], lo[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float a = exp2f(s[c * 8 + 2 * e] - m_run);
-                    const float b = exp2f(s[c * 8 + 2 * e + 1] - m_run);
-                    l_run += a + b;
-                    split2<T>(a, b, hi[e], lo[e]);
+                // Tokens past the sequence end in this tile: zero their V rows
+                // (unwritten slots may hold NaN; 0 * NaN must not reach O).
+                // Done before P(g) is published, which precedes PV(g).
+                const uint64_t t0 = static_cast<uint64_t>(j) * kBN;
+                if (t0 + kBN > p.kv_tokens) {
+                    const uint32_t sv = g % kVStages;
+                    if (!wait_all(&v_full[sv], (g / kVStages) & 1u)) { ok = false; break; }
+                    const uint32_t valid = static_cast<uint32_t>(p.kv_tokens - t0);
+                    const uint32_t rows = kBN - valid;
+                    unsigned char* vt = smem + kOffV + sv * kKVTile;
+                    for (uint32_t i = r; i < rows * 2 * 8; i += 128) {
+                        const uint32_t row = valid + i / 16, half = (i / 8) & 1, cc = i & 7;
+                        *reinterpret_cast<uint4*>(vt + half * kKVHalf + row * 128 + cc * 16) =
+                            make_uint4(0, 0, 0, 0);
+                    }
+                    fence_proxy_async_smem();
                 }
-                const uint32_t off = swz_row(r, c);
-                *reinterpret_cast<uint4*>(phi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4*>(plo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                tc::fence_before_sync();
+                mbar_arrive(&p_full[b]);
             }
-            // Tokens past the sequence end in this tile: zero their V rows
-            // (unwritten slots may hold NaN; 0 * NaN must not reach O).
-            if (t0 + kBN > p.kv_tokens) {
-                const uint32_t valid = static_cast<uint32_t>(p.kv_tokens - t0);
-                const uint32_t rows = kBN - valid;
-                unsigned char* vt = smem + kOffV + (j % kStages) * kKVTile;
-                for (uint32_t x = r; x < rows * 2 * 8; x += 128) {
-                    const uint32_t row = valid + x / 16, half = (x / 8) & 1, c = x & 7;
-                    *reinterpret_cast<uint4*>(vt + half * kKVHalf + row * 128 + c * 16) = make_uint4(0, 0, 0, 0);
-                }
-            }
-            fence_proxy_async_smem();
-            tc::fence_before_sync();
-            mbar_arrive(&p_full);
-        }
-        if (ok && ntiles > 0 && wait_all(&o_done, (ntiles - 1) & 1u)) {
+            if (!ok) break;
+            // Epilogue of the unit: O / l to global memory, then O is free.
+            if (!wait_all(&o_full, k & 1u)) break;
             tc::fence_after_sync();
             const float inv = 1.f / l_run;
-            float* orow = p.o + (qi * p.q_heads + qh) * kHD;
+            const uint64_t qi = u.q0 + r;
+            const bool row_live = qi < p.q_tokens;
+            float* orow = p.o + (qi * p.q_heads + u.qh) * kHD;
 #pragma unroll 1
             for (int cb = 0; cb < kHD; cb += 32) {
                 float ov[32];
-                tc::ld32(tO + lane_base + cb, ov);
-                tc::wait_ld();
+                tc::ld32(tO + cb, ov);
+                tc::wait_ld32(ov);
                 if (row_live) {
 #pragma unroll
                     for (int e = 0; e < 32; e += 4) {
@@ -358,8 +478,47 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
                     }
                 }
             }
-        } else if (!ok) {
-            abort_flag = 1;
+            tc::fence_before_sync();
+            mbar_arrive(&o_free);
+        }
+    } else if (warp >= 8) {
+        // ----------------------------------------------------- Q staging ---
+        const uint32_t r = static_cast<uint32_t>(tid - 256);  // row within the unit
+        unsigned char* qhi = smem + kOffQ;
+        unsigned char* qlo = qhi + kQBytes;
+        Unit u;
+        for (uint32_t round = 0, k = 0; unit_at(p, round, u); ++round, ++k) {
+            const uint64_t qi = u.q0 + r;
+            const bool row_live = qi < p.q_tokens;
+            float v[kHD];
+            if (row_live) {
+                const float4* qrow = reinterpret_cast<const float4*>(p.q + (qi * p.q_heads + u.qh) * kHD);
+#pragma unroll
+                for (int e = 0; e < kHD / 4; ++e) {
+                    const float4 x = __ldg(qrow + e);
+                    v[4 * e] = x.x;
+                    v[4 * e + 1] = x.y;
+                    v[4 * e + 2] = x.z;
+                    v[4 * e + 3] = x.w;
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < kHD; ++e) v[e] = 0.f;
+            }
+            // The previous unit's last QK has read the Q tile.
+            if (k >= 1 && !mbar_wait_lean(&q_free, (k - 1) & 1u, p.status)) break;
+#pragma unroll
+            for (uint32_t cc = 0; cc < kHD / 8; ++cc) {
+                uint32_t hi[4], lo[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    split2_fast<T>(v[8 * cc + 2 * e] * p.qscale, v[8 * cc + 2 * e + 1] * p.qscale, hi[e], lo[e]);
+                const uint32_t off = (cc >> 3) * kQAtom + swz_row(r, cc & 7);
+                *reinterpret_cast<uint4*>(qhi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4*>(qlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&q_full);
         }
     }
 
@@ -375,7 +534,7 @@ bool prefill_eligible(const CacheView& c, const AttentionArgs& a) {
     return (c.dtype == KVFX_BF16 || c.dtype == KVFX_F16) && c.bs == 16 && c.hd == kHD && a.query_tokens >= 2 &&
            a.q_heads % c.heads == 0 && c.num_blocks < (1ull << 31) &&
            reinterpret_cast<uintptr_t>(a.q) % 16 == 0 && reinterpret_cast<uintptr_t>(a.o) % 16 == 0 &&
-           ceil_div(a.query_tokens, kBM) < (1ull << 31) && a.q_heads <= 65535;
+           ceil_div(a.query_tokens, kBM) < (1ull << 31);
 }
 
 }  // namespace
@@ -397,6 +556,8 @@ cudaError_t launch_prefill_tc(const CacheView& c, const AttentionArgs& a, unsign
         if (err != cudaSuccess) return err;
         if (c.device >= 0 && c.device < 64) attr_done[c.device] = true;
     }
+    const int sms = device_sm_count(c.device);
+    if (sms <= 0) return cudaErrorInvalidDevice;
     PrefillParams p;
     p.q = a.q;
     p.o = a.o;
@@ -408,9 +569,10 @@ cudaError_t launch_prefill_tc(const CacheView& c, const AttentionArgs& a, unsign
     p.kv_heads = c.heads;
     p.group = a.q_heads / c.heads;
     p.n_qtiles = static_cast<uint32_t>(ceil_div(a.query_tokens, kBM));
+    p.n_units = static_cast<uint64_t>(p.n_qtiles) * a.q_heads;
     p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.hd)));
     p.status = status;
-    dim3 grid(p.n_qtiles, a.q_heads, 1);
+    const unsigned grid = static_cast<unsigned>(umin64(p.n_units, static_cast<uint64_t>(sms)));
     if (bf) {
         prefill_tc_kernel<__nv_bfloat16><<<grid, kThreads, kSmemAlloc, s>>>(p, maps->k, maps->v);
     } else {

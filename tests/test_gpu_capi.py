@@ -217,6 +217,29 @@ def test_decode_split_k_merge(pps):
     assert float(np.abs(out.cpu().numpy() - exp).max()) < TOL["bfloat16"]
 
 
+@pytest.mark.parametrize("dtype,pps", [("bfloat16", 8), ("bfloat16", 0), ("float16", 64)])
+def test_decode_rescale_path(dtype, pps):
+    """Q scaled by 8 (scores with ~8x the spread): running maxima rise by more
+    than the lazy-rescale threshold inside splits, and splits with very
+    different maxima are merged."""
+    lens = [3000, 700, 129, 4100]
+    c, table, lens_np, q, qh = _decode_case(dtype, 128, 16, 4, 4, lens, seed=91)
+    q = q * np.float32(8.0)
+    batch, max_len = len(lens), int(lens_np.max())
+    ws_bytes = kv.lib.kvfx_decode_workspace_bytes(ctypes.byref(c.desc), batch, qh, max_len, pps)
+    ws = torch.zeros(max(int(ws_bytes), 16), dtype=torch.uint8, device="cuda")
+    qd = torch.from_numpy(q).cuda()
+    out = torch.empty(batch * qh * 128, device="cuda")
+    call(kv.lib.kvfx_decode, ctypes.byref(c.desc), qd.data_ptr(), out.data_ptr(), u64(table),
+         u64(lens_np), batch, table.shape[1], qh, max_len, pps, ws.data_ptr(), ws.numel(), None)
+    exp = oracle.decode_batch(c.host_k, c.host_v, w.DTYPE_CODE[dtype], c.nb, 4, 16, 128, table, lens_np, qh, q,
+                              threads=8)
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert float(np.abs(got - exp).max()) < TOL[dtype]
+    assert kv.device_status(0) == 0
+
+
 @pytest.mark.parametrize("dtype,hd,bs,kvh,group,lq,kvlen", [
     ("bfloat16", 128, 16, 2, 4, 1, 300), ("bfloat16", 128, 16, 2, 4, 37, 300), ("float32", 4, 4, 2, 2, 10, 10),
     ("float16", 64, 16, 1, 8, 64, 64), ("float32", 3, 2, 3, 1, 5, 9)])
@@ -269,15 +292,20 @@ def test_workspace_too_small_is_rejected():
 
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
-@pytest.mark.parametrize("kvh,group,lq,kvlen", [(2, 4, 2, 2), (1, 8, 127, 127), (2, 1, 128, 128), (2, 4, 129, 129),
-                                                (1, 4, 300, 300), (2, 4, 100, 333), (1, 2, 64, 1000)])
-def test_prefill_tensor_core_path(dtype, kvh, group, lq, kvlen):
+@pytest.mark.parametrize("kvh,group,lq,kvlen,qmul", [
+    (2, 4, 2, 2, 1.0), (1, 8, 127, 127, 1.0), (2, 1, 128, 128, 1.0), (2, 4, 129, 129, 1.0), (1, 4, 300, 300, 1.0),
+    (2, 4, 100, 333, 1.0), (1, 2, 64, 1000, 1.0), (2, 3, 200, 517, 1.0), (2, 2, 256, 256, 1.0),
+    # Scores with ~8x the spread: running row maxima rise by more than 8
+    # (base 2) after the first tile, so O is rescaled in TMEM.
+    (1, 4, 300, 300, 8.0), (2, 3, 96, 700, 8.0)])
+def test_prefill_tensor_core_path(dtype, kvh, group, lq, kvlen, qmul):
     """Causal prefill on the tcgen05 kernel (16-bit cache, head_size 128,
     block 16): suffix-aligned queries, partial query and KV tiles, NaN-poisoned
-    slots past the sequence end; max |err| against the FP64 oracle."""
+    slots past the sequence end, paired (even group) and single Q tiles per
+    CTA; max |err| against the FP64 oracle."""
     c, table, _, _, qh = _decode_case(dtype, 128, 16, kvh, group, [kvlen], seed=lq * 7 + kvlen + group)
     blocks = table[0]
-    q = w.normal(lq + 11 * kvlen, lq * qh * 128)
+    q = w.normal(lq + 11 * kvlen, lq * qh * 128) * np.float32(qmul)
     qd = torch.from_numpy(q).cuda()
     out = torch.full((lq * qh * 128 + 1,), 12345.0, device="cuda")
     call(kv.lib.kvfx_attention, ctypes.byref(c.desc), qd.data_ptr(), out.data_ptr(), u64(blocks), lq, kvlen, qh,
@@ -290,6 +318,30 @@ def test_prefill_tensor_core_path(dtype, kvh, group, lq, kvlen):
     assert err < TOL[dtype], err
     assert got[-1] == 12345.0
     assert kv.device_status(0) == 0
+    if qmul > 1:
+        assert _rescaled_rows(c, dtype, blocks, lq, kvlen, kvh, group, q) > 0
+
+
+def _rescaled_rows(c, dtype, blocks, lq, kvlen, kvh, group, q, tile=64):
+    """Rows (x heads) whose score maximum over some later 64-token tile exceeds
+    the first tile's by more than 8 in base 2: the cases that take the
+    kernel's O-rescale path."""
+    raw = c.host_k.view(np.uint16).reshape(c.nb, kvh, 16, 128)
+    f = (raw.astype(np.uint32) << 16).view(np.float32) if dtype == "bfloat16" else \
+        raw.view(np.float16).astype(np.float32)
+    npg = (kvlen + 15) // 16
+    keys = f[blocks[:npg].astype(np.int64)].transpose(1, 0, 2, 3).reshape(kvh, -1, 128)[:, :kvlen]
+    qh = kvh * group
+    qs = q.reshape(lq, qh, 128).astype(np.float64)
+    pos = kvlen - lq + np.arange(lq)
+    count = 0
+    for h in range(qh):
+        s = qs[:, h] @ keys[h // group].T.astype(np.float64) * (1.4426950408889634 / np.sqrt(128.0))
+        s[np.arange(kvlen)[None, :] > pos[:, None]] = -np.inf
+        first = s[:, :tile].max(axis=1)
+        later = s[:, tile:].max(axis=1) if kvlen > tile else np.full(lq, -np.inf)
+        count += int((later > first + 8).sum())
+    return count
 
 
 def test_prefill_long_sequence_sampled_rows():
