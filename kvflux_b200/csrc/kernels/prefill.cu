@@ -54,6 +54,9 @@ constexpr int kSBufs = 3;        // S/P buffers in TMEM
 constexpr int kThreads = 384;    // 12 warps
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemO = kSBufs * kBN;          // O accumulator column
+// The producers' waits on s_full / pv_done rely on a ring of no more slots
+// than there are S buffers (see produce()).
+static_assert(kKStages <= kSBufs && kVStages <= kSBufs, "ring deeper than the S buffers");
 
 // Shared-memory layout (byte offsets from a 1024-aligned base).
 constexpr uint32_t kQAtom = kBM * 128;             // [128 rows][64 dims] 16-bit, 16 KiB
@@ -136,14 +139,22 @@ __device__ __forceinline__ uint32_t swz_row(uint32_t r, uint32_t c) {
     return (r >> 3) * 1024 + (r & 7) * 128 + (((c ^ r) & 7) << 4);
 }
 
-// One KV tile (8 pages of one KV head) into a ring slot.
-__device__ __forceinline__ void load_kv_tile(const PrefillParams& p, const CUtensorMap* map, unsigned char* dst,
-                                             uint32_t kh, uint32_t j, uint64_t npages, uint64_t* bar) {
-    mbar_arrive_expect_tx(bar, kKVTile);
-#pragma unroll 2
+// Page ids of KV tile j (8 pages), loaded together: one memory round trip.
+__device__ __forceinline__ void tile_pages(const PrefillParams& p, uint32_t j, uint64_t npages, uint64_t* ids) {
+#pragma unroll
     for (int pg = 0; pg < kBN / 16; ++pg) {
         const uint64_t lp = static_cast<uint64_t>(j) * (kBN / 16) + pg;
-        uint64_t blk = __ldg(p.blocks + (lp < npages ? lp : 0));
+        ids[pg] = __ldg(p.blocks + (lp < npages ? lp : 0));
+    }
+}
+
+// One KV tile (8 pages of one KV head) into a ring slot.
+__device__ __forceinline__ void load_kv_tile(const PrefillParams& p, const CUtensorMap* map, unsigned char* dst,
+                                             uint32_t kh, const uint64_t* ids, uint64_t* bar) {
+    mbar_arrive_expect_tx(bar, kKVTile);
+#pragma unroll
+    for (int pg = 0; pg < kBN / 16; ++pg) {
+        uint64_t blk = ids[pg];
         if (blk >= p.num_blocks) {
             raise_flag(p.status, KVFX_FLAG_BAD_INDEX);
             blk = 0;
@@ -156,19 +167,31 @@ __device__ __forceinline__ void load_kv_tile(const PrefillParams& p, const CUten
     }
 }
 
-// Producer loop of one ring (K or V): waits for the slot's previous tile to be
-// consumed, loads the next, then waits for its own copies in flight.
+// Producer loop of one ring (K or V) of `kStages` slots: before tile g is
+// loaded into slot g % kStages, the MMA that read tile g - kStages must have
+// completed, which the MMA thread's commit to done[(g - kStages) % kSBufs]
+// signals (s_full for K: QK(g) completes; pv_done for V: PV(g) completes).
+// Neither barrier can run a phase ahead: tile g's own MMA needs this load.
+// The next tile's page ids are fetched while waiting for its slot. At the
+// end, waits for its own copies in flight.
 __device__ __noinline__ void produce(const PrefillParams& p, const CUtensorMap* map, unsigned char* ring,
-                                     uint64_t* full, uint64_t* empty, uint64_t npages, uint32_t kStages) {
+                                     uint64_t* full, uint64_t* done, uint64_t npages, uint32_t kStages) {
     prefetch_tensormap(map);
     TileCursor c;
     c.init(p);
+    uint64_t ids[kBN / 16];
+    if (c.valid) tile_pages(p, c.j, npages, ids);
     uint32_t issued = 0;
-    for (; c.valid; c.next(p)) {
+    while (c.valid) {
         const uint32_t g = c.g, st = g % kStages;
-        if (g >= kStages && !mbar_wait_lean(&empty[st], ((g / kStages) - 1) & 1u, p.status)) break;
-        load_kv_tile(p, map, ring + st * kKVTile, c.u.kh, c.j, npages, &full[st]);
+        if (g >= kStages) {
+            const uint32_t prev = g - kStages;
+            if (!mbar_wait_lean(&done[prev % kSBufs], (prev / kSBufs) & 1u, p.status)) break;
+        }
+        load_kv_tile(p, map, ring + st * kKVTile, c.u.kh, ids, &full[st]);
         issued = g + 1;
+        c.next(p);
+        if (c.valid) tile_pages(p, c.j, npages, ids);
     }
     for (uint32_t g = issued > kStages ? issued - kStages : 0; g < issued; ++g)
         (void)mbar_wait_lean(&full[g % kStages], (g / kStages) & 1u, p.status);
@@ -179,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap) {
     extern __shared__ unsigned char smem_raw[];
-    __shared__ uint64_t k_full[kKStages], k_empty[kKStages], v_full[kVStages], v_empty[kVStages];
+    __shared__ uint64_t k_full[kKStages], v_full[kVStages];
     __shared__ uint64_t s_full[kSBufs], p_full[kSBufs], pv_done[kSBufs];
     __shared__ uint64_t q_full, q_free, o_full, o_free, mma_done;
     __shared__ uint32_t tmem_base_slot;
@@ -191,14 +214,8 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
     const uint64_t npages = ceil_div(p.kv_tokens, 16);
 
     if (tid == 0) {
-        for (int s = 0; s < kKStages; ++s) {
-            mbar_init(&k_full[s], 1);
-            mbar_init(&k_empty[s], 1);
-        }
-        for (int s = 0; s < kVStages; ++s) {
-            mbar_init(&v_full[s], 1);
-            mbar_init(&v_empty[s], 1);
-        }
+        for (int s = 0; s < kKStages; ++s) mbar_init(&k_full[s], 1);
+        for (int s = 0; s < kVStages; ++s) mbar_init(&v_full[s], 1);
         for (int b = 0; b < kSBufs; ++b) {
             mbar_init(&s_full[b], 1);
             mbar_init(&p_full[b], 128);
@@ -222,10 +239,10 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
 
     if (warp == 0) {
         // ---------------------------------------------------- K producer ---
-        if (lane == 0) produce(p, &kmap, smem + kOffK, k_full, k_empty, npages, kKStages);
+        if (lane == 0) produce(p, &kmap, smem + kOffK, k_full, s_full, npages, kKStages);
     } else if (warp == 2) {
         // ---------------------------------------------------- V producer ---
-        if (lane == 0) produce(p, &vmap, smem + kOffV, v_full, v_empty, npages, kVStages);
+        if (lane == 0) produce(p, &vmap, smem + kOffV, v_full, pv_done, npages, kVStages);
     } else if (warp == 1) {
         // ----------------------------------------------------- MMA issuer ---
         if (lane == 0) {
@@ -241,58 +258,93 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
             TileCursor qk, pv;
             qk.init(p);
             pv.init(p);
-            // S(g) = Q K_g^T into S[g%3]; S[g%3] held P(g-3) until PV(g-3) completed.
-            auto issue_qk = [&]() -> bool {
-                const uint32_t g = qk.g, b = g % kSBufs, st = g % kKStages;
+            // S(g) = Q K_g^T into S[g%3]; S[g%3] held P(g-3) until PV(g-3)
+            // completed. Each step is split into its waits, its 16 MMAs and
+            // its commits, so that the next step's waits can run while the
+            // tensor pipe still has this step's last MMAs queued.
+            auto qk_wait = [&]() -> bool {
+                const uint32_t g = qk.g;
                 if (qk.j == 0 && !mbar_wait_lean(&q_full, qk.k & 1u, p.status)) return false;
-                if (!mbar_wait_lean(&k_full[st], (g / kKStages) & 1u, p.status)) return false;
-                if (g >= kSBufs && !mbar_wait_lean(&pv_done[b], ((g / kSBufs) - 1) & 1u, p.status)) return false;
+                if (!mbar_wait_lean(&k_full[g % kKStages], (g / kKStages) & 1u, p.status)) return false;
+                if (g >= kSBufs && !mbar_wait_lean(&pv_done[g % kSBufs], ((g / kSBufs) - 1) & 1u, p.status))
+                    return false;
                 tc::fence_after_sync();
-                const uint32_t d = tmem + b * kBN;
-                const uint64_t k_desc = k_desc0 + ((st * kKVTile) >> 4);
-                // 16 MMAs: Q_hi then Q_lo, 8 K-steps of 16 each (unrolled: the
-                // constant operand offsets fold into the descriptor adds).
+                return true;
+            };
+            auto qk_mmas = [&](uint32_t from, uint32_t to) {
+                const uint32_t g = qk.g;
+                const uint32_t d = tmem + (g % kSBufs) * kBN;
+                const uint64_t k_desc = k_desc0 + (((g % kKStages) * kKVTile) >> 4);
+                // Q_hi then Q_lo, 8 K-steps of 16 each (unrolled: the constant
+                // operand offsets fold into the descriptor adds).
 #pragma unroll
                 for (uint32_t i = 0; i < 16; ++i) {
+                    if (i < from || i >= to) continue;
                     const uint32_t part = i >> 3, kk = i & 7;
                     const uint32_t a_off = part * kQBytes + (kk >> 2) * kQAtom + (kk & 3) * 32;
                     const uint32_t b_off = (kk >> 2) * kKVHalf + (kk & 3) * 32;
                     tc::mma(d, q_desc0 + (a_off >> 4), k_desc + (b_off >> 4), id_qk, i > 0 ? 1u : 0u);
                 }
-                tc::commit(&s_full[b]);
-                tc::commit(&k_empty[st]);
+            };
+            auto qk_finish = [&]() {
+                tc::commit(&s_full[qk.g % kSBufs]);
                 if (qk.last()) tc::commit(&q_free);  // Q may be replaced once this completes
                 qk.next(p);
-                return true;
             };
             // O += P(g) V_g with P from TMEM; a unit's first PV overwrites O,
             // which the previous unit's epilogue must have read.
-            auto issue_pv = [&]() -> bool {
-                const uint32_t g = pv.g, b = g % kSBufs, sv = g % kVStages;
+            auto pv_wait = [&]() -> bool {
+                const uint32_t g = pv.g;
                 if (pv.j == 0 && pv.k >= 1 && !mbar_wait_lean(&o_free, (pv.k - 1) & 1u, p.status)) return false;
-                if (!mbar_wait_lean(&v_full[sv], (g / kVStages) & 1u, p.status)) return false;
-                if (!mbar_wait_lean(&p_full[b], (g / kSBufs) & 1u, p.status)) return false;
+                if (!mbar_wait_lean(&v_full[g % kVStages], (g / kVStages) & 1u, p.status)) return false;
+                if (!mbar_wait_lean(&p_full[g % kSBufs], (g / kSBufs) & 1u, p.status)) return false;
                 tc::fence_after_sync();
-                const uint32_t pt = tmem + b * kBN;
-                const uint64_t v_desc = v_desc0 + ((sv * kKVTile) >> 4);
-                // 16 MMAs: 8 K-steps of 16 tokens, P_hi then P_lo for each.
+                return true;
+            };
+            auto pv_mmas = [&](uint32_t from, uint32_t to) {
+                const uint32_t g = pv.g;
+                const uint32_t pt = tmem + (g % kSBufs) * kBN;
+                const uint64_t v_desc = v_desc0 + (((g % kVStages) * kKVTile) >> 4);
+                // 8 K-steps of 16 tokens, P_hi then P_lo for each.
 #pragma unroll
                 for (uint32_t i = 0; i < 16; ++i) {
+                    if (i < from || i >= to) continue;
                     const uint32_t t = i >> 1, part = i & 1;
                     const uint32_t a = pt + (t >> 1) * 32 + part * 16 + (t & 1) * 8;
                     tc::mma_ts(tmem + kTmemO, a, v_desc + ((t * 2048) >> 4), id_pv, (pv.j > 0 || i > 0) ? 1u : 0u);
                 }
-                tc::commit(&pv_done[b]);
-                tc::commit(&v_empty[sv]);
+            };
+            auto pv_finish = [&]() {
+                tc::commit(&pv_done[pv.g % kSBufs]);
                 if (pv.last()) tc::commit(&o_full);
                 pv.next(p);
-                return true;
             };
+            constexpr uint32_t kSplit = 12;  // MMAs of a step issued before the next step's waits
             bool ok = true;
-            for (int i = 0; i < 2 && ok && qk.valid; ++i) ok = issue_qk();
+            for (int i = 0; i < 2 && ok && qk.valid; ++i) {  // QK(0), QK(1)
+                ok = qk_wait();
+                if (ok) {
+                    qk_mmas(0, 16);
+                    qk_finish();
+                }
+            }
+            if (ok && pv.valid) ok = pv_wait();
+            // Steady state: PV(g), then QK(g + 2).
             while (ok && pv.valid) {
-                ok = issue_pv();
-                if (ok && qk.valid) ok = issue_qk();
+                pv_mmas(0, kSplit);
+                const bool more_qk = qk.valid;
+                if (more_qk) ok = qk_wait();
+                pv_mmas(kSplit, 16);
+                pv_finish();
+                if (!ok) break;
+                if (more_qk) {
+                    qk_mmas(0, kSplit);
+                    if (pv.valid) ok = pv_wait();
+                    qk_mmas(kSplit, 16);
+                    qk_finish();
+                } else if (pv.valid) {
+                    ok = pv_wait();
+                }
             }
             // Every MMA this thread issued is complete before TMEM is released.
             tc::commit(&mma_done);
