@@ -1,6 +1,6 @@
 // Device-side helpers shared by the sm_100a kernels: element types, the
 // status word, bounded waits, and thin inline-PTX wrappers for mbarrier,
-// bulk/tensor TMA copies, ldmatrix and mma.sync.
+// bulk/tensor TMA loads, ldmatrix and mma.sync.
 #pragma once
 
 #include <cuda.h>
@@ -123,27 +123,6 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
         : "memory");
 }
 
-// 1-D bulk copy shared -> global in the issuing thread's bulk async-group.
-__device__ __forceinline__ void bulk_s2g(void* gmem_dst, const void* smem_src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
-                 ::"l"(gmem_dst), "r"(smem_addr(smem_src)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void bulk_commit() {
-    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-
-// Wait until at most N of this thread's bulk groups still read shared memory.
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() {
-    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-
-template <int N>
-__device__ __forceinline__ void bulk_wait_all() {
-    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // Tiled 4-D tensor load (no multicast) into shared memory, completion on `bar`.
 __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, int c0, int c1,
                                             int c2, int c3, uint64_t* bar) {
@@ -157,19 +136,6 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
-}
-
-// Per-thread register budget of the executing warpgroup (all 128 threads
-// execute it together). The increases of all warpgroups must fit in what
-// the block was launched with (threads x registers per thread), or an
-// increase waits for registers that are never released.
-template <uint32_t N>
-__device__ __forceinline__ void regs_increase() {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
-}
-template <uint32_t N>
-__device__ __forceinline__ void regs_decrease() {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ------------------------------------------------------------ tensor ops ---

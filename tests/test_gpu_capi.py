@@ -146,12 +146,29 @@ def test_copy_page_byte_exact(dtype, hd, bs, heads):
     assert kv.lib.kvfx_copy_page(ctypes.byref(c.desc), 3, 16, None) == kv.KVFX_ERANGE
 
 
-def _decode_case(dtype, hd, bs, kvh, group, lens, seed, pps=0, poison_tail=True):
+def _page_order(order, nb, seed):
+    """Physical page ids handed out in order: "perm" (fragmented), "seq" (one
+    run from page 0, as a fresh free list gives them), "mixed" (runs ending on
+    the pool's last page, some broken by a swapped pair, some reversed)."""
+    if order == "perm":
+        return w.permutation(seed, np.arange(nb))
+    ids = np.arange(nb)
+    if order == "mixed":
+        ids = np.roll(ids, -8)  # the runs that reach the end of the pool wrap to page 0
+        for t in range(0, nb // 8):
+            if t % 3 == 1:
+                ids[8 * t + 3], ids[8 * t + 4] = ids[8 * t + 4], ids[8 * t + 3]
+            elif t % 3 == 2:
+                ids[8 * t:8 * t + 8] = ids[8 * t:8 * t + 8][::-1].copy()
+    return ids
+
+
+def _decode_case(dtype, hd, bs, kvh, group, lens, seed, pps=0, poison_tail=True, order="perm"):
     c = Cache(int(sum((l + bs - 1) // bs for l in lens)) + 8, kvh, bs, hd, dtype, seed=seed)
     qh = kvh * group
     batch = len(lens)
     width = max((l + bs - 1) // bs for l in lens)
-    ids = w.permutation(seed + 3, np.arange(c.nb))
+    ids = _page_order(order, c.nb, seed + 3)
     table = np.full((batch, width), 2**64 - 1, np.uint64)
     k = 0
     for r, l in enumerate(lens):
@@ -298,12 +315,15 @@ def test_workspace_too_small_is_rejected():
     # Scores with ~8x the spread: running row maxima rise by more than 8
     # (base 2) after the first tile, so O is rescaled in TMEM.
     (1, 4, 300, 300, 8.0), (2, 3, 96, 700, 8.0)])
-def test_prefill_tensor_core_path(dtype, kvh, group, lq, kvlen, qmul):
+@pytest.mark.parametrize("order", ["perm", "seq", "mixed"])
+def test_prefill_tensor_core_path(dtype, kvh, group, lq, kvlen, qmul, order):
     """Causal prefill on the tcgen05 kernel (16-bit cache, head_size 128,
     block 16): suffix-aligned queries, partial query and KV tiles, NaN-poisoned
-    slots past the sequence end, paired (even group) and single Q tiles per
-    CTA; max |err| against the FP64 oracle."""
-    c, table, _, _, qh = _decode_case(dtype, 128, 16, kvh, group, [kvlen], seed=lq * 7 + kvlen + group)
+    slots past the sequence end, GQA groups 1..8, pages fragmented or in
+    consecutive runs as a free list hands them out; max |err| against the
+    FP64 oracle."""
+    c, table, _, _, qh = _decode_case(dtype, 128, 16, kvh, group, [kvlen], seed=lq * 7 + kvlen + group,
+                                      order=order)
     blocks = table[0]
     q = w.normal(lq + 11 * kvlen, lq * qh * 128) * np.float32(qmul)
     qd = torch.from_numpy(q).cuda()
