@@ -8,6 +8,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <functional>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -66,9 +67,22 @@ struct StorageRuntime {
     // Copies `n` arrays (host pointers and byte counts) into device scratch
     // with one H2D copy on the legacy default stream; returns device pointers.
     void upload(const void* const* host, const std::size_t* bytes, int n, void** device_out);
+    // The two halves of upload for callers that write straight into the
+    // staging: stage() sizes pinned staging and device scratch for `n`
+    // arrays (each at a 256-byte aligned offset) and returns the host and
+    // device addresses of each; push() issues the one H2D copy.
+    void stage(const std::size_t* bytes, int n, void** host_out, void** device_out);
+    void push();
+    std::size_t staged_bytes = 0;
     void* ensure_workspace(std::size_t bytes);
     // Synchronises the legacy default stream and raises on device-side flags.
     void finish(const char* op) const;
 };
+
+// Runs fn(begin, end) over [0, n) in chunks of `grain` on a small pool of
+// persistent host threads plus the caller (inline when n <= grain). fn must
+// be safe to run concurrently on disjoint ranges; the call returns when all
+// chunks are done.
+void parallel_for(std::size_t n, std::size_t grain, const std::function<void(std::size_t, std::size_t)>& fn);
 
 } // namespace kvflux::v2::detail

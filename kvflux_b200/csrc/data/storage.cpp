@@ -63,7 +63,7 @@ StorageRuntime::~StorageRuntime() {
     (void)cudaSetDevice(prev);
 }
 
-void StorageRuntime::upload(const void* const* host, const std::size_t* bytes, int n, void** device_out) {
+void StorageRuntime::stage(const std::size_t* bytes, int n, void** host_out, void** device_out) {
     std::size_t total = 0;
     std::size_t offsets[8];
     for (int i = 0; i < n; ++i) {
@@ -86,15 +86,27 @@ void StorageRuntime::upload(const void* const* host, const std::size_t* bytes, i
         cuda_check(cudaMalloc(&dev_scratch, cap), "allocate device scratch");
         dev_bytes = cap;
     }
-    auto* staging = static_cast<unsigned char*>(pinned);
     for (int i = 0; i < n; ++i) {
-        if (bytes[i] != 0) std::memcpy(staging + offsets[i], host[i], bytes[i]);
+        host_out[i] = static_cast<unsigned char*>(pinned) + offsets[i];
         device_out[i] = static_cast<unsigned char*>(dev_scratch) + offsets[i];
     }
+    staged_bytes = total;
+}
+
+void StorageRuntime::push() {
     // The staging buffer is reused by the next call only after this call has
     // synchronised the stream, so one buffer suffices.
-    cuda_check(cudaMemcpyAsync(dev_scratch, pinned, total, cudaMemcpyHostToDevice, nullptr),
+    cuda_check(cudaMemcpyAsync(dev_scratch, pinned, staged_bytes, cudaMemcpyHostToDevice, nullptr),
                "upload tables");
+}
+
+void StorageRuntime::upload(const void* const* host, const std::size_t* bytes, int n, void** device_out) {
+    void* staging[8];
+    stage(bytes, n, staging, device_out);
+    for (int i = 0; i < n; ++i) {
+        if (bytes[i] != 0) std::memcpy(staging[i], host[i], bytes[i]);
+    }
+    push();
 }
 
 void* StorageRuntime::ensure_workspace(std::size_t bytes) {

@@ -59,6 +59,19 @@ def test_config3_decode_all_rows(cuda):
     _decode_vs_oracle(wl, list(range(wl.batch)), 2e-3)
 
 
+def test_config3_api_matches_capi(cuda):
+    """paged_attention_batch (host table written in parallel into pinned
+    staging) against the C-ABI launch on the same table: bit-identical."""
+    wl = bench.Decode(kv, w, w.CONFIG3, 0, 1)
+    wl.launch(None)
+    torch.cuda.synchronize()
+    ref = wl.o.clone()
+    wl.o.fill_(12345.0)
+    kv.paged_attention_batch(wl.storage, wl.b.sequences, wl.q, wl.o, wl.qh)
+    assert torch.equal(wl.o, ref)
+    assert kv.device_status(0) == 0
+
+
 def test_config5_decode_sampled_rows(cuda):
     wl = bench.Decode(kv, w, w.CONFIG5, 0, 1)
     lens = wl.lens
