@@ -86,8 +86,10 @@ def test_write_byte_exact(dtype, hd, bs, heads):
     assert kv.device_status(0) == 0
 
 
+# Rows of 16-byte multiples take the direct page kernel (16 heads of 128 bf16:
+# a 64 KiB page), other rows the SIMT one.
 @pytest.mark.parametrize("dtype,hd,bs,heads", [("bfloat16", 128, 16, 8), ("float16", 64, 16, 4), ("float32", 3, 4, 2),
-                                               ("float32", 32, 16, 2), ("bfloat16", 5, 8, 3)])
+                                               ("float32", 32, 16, 2), ("bfloat16", 5, 8, 3), ("bfloat16", 128, 16, 16)])
 @pytest.mark.parametrize("length", [1, 15, 16, 17, 333])
 def test_gather_byte_exact_with_sentinel(dtype, hd, bs, heads, length):
     c = Cache(128, heads, bs, hd, dtype, seed=31)
