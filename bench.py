@@ -618,7 +618,11 @@ def only_case(args, ranks: Ranks, kv, w, peak: float) -> int:
                "tflops": pf.flops / (ms * 1e-3) / 1e12, "gbs": 0.0}
         out["frac_of_bf16_peak"] = out["tflops"] / load_bf16_peak()[0]
     else:
-        wg = WriteGather(kv, w, w.CONFIG2, ranks.rank, ranks.world)
+        cfg = dict(w.CONFIG2)
+        if args.batch:  # fewer sequences on a proportionally smaller pool
+            cfg["pool_pages"] = max(1, cfg["pool_pages"] * args.batch // cfg["sequences"])
+            cfg["sequences"] = args.batch
+        wg = WriteGather(kv, w, cfg, ranks.rank, ranks.world)
         fn = wg.write if args.only == "write" else wg.gather
         per, total = time_launches(fn, args.steps, args.warmup, ranks)
         ms = total / args.steps
@@ -645,7 +649,7 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather", "prefill4"],
                     help="run one kernel's case alone (profiling runs); prints a short JSON line")
-    ap.add_argument("--batch", type=int, default=None, help="override the decode batch (profiling runs)")
+    ap.add_argument("--batch", type=int, default=None, help="override the batch: decode requests, write/gather sequences (profiling runs)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
