@@ -79,6 +79,11 @@ public:
 
     Stats stats() const noexcept;
     std::size_t capacity() const noexcept { return slots_.size(); }
+    // Hint: bring the bookkeeping of `h` into cache ahead of a lookup. No
+    // check, no effect on state.
+    void prefetch(BlockHandle h) const noexcept {
+        if (h.id < slots_.size()) __builtin_prefetch(slots_.data() + h.id);
+    }
     std::size_t block_size() const noexcept { return block_size_; }
     // FNV-1a (64-bit) over each token's four bytes, least significant first.
     static std::uint64_t prefix_hash(const Tokens& prefix) noexcept;

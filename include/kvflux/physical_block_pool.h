@@ -33,6 +33,7 @@ public:
 
     // Only a live handle yields an id; a stale generation throws invalid_argument.
     PhysicalBlockID id(PhysicalBlockHandle handle) const;
+    void prefetch(PhysicalBlockHandle handle) const noexcept { manager_.prefetch(handle); }
     std::size_t ref_count(PhysicalBlockHandle handle) const;
     std::size_t capacity() const noexcept;
     std::size_t block_size() const noexcept;

@@ -34,6 +34,11 @@ public:
     PhysicalBlockID operator[](std::size_t logical_block) const {
         return physical_id(logical_block);
     }
+    // out[j] = physical_id(j) for every entry (the same checks and
+    // exceptions, in entry order), with the pool's bookkeeping of entry
+    // j + 16 prefetched while entry j is checked: entries are random pages,
+    // so one lookup after another would wait on a cache miss each.
+    void copy_ids(PhysicalBlockID* out) const;
     std::size_t size() const noexcept { return entries_.size(); }
     bool empty() const noexcept { return entries_.empty(); }
     bool shares_pool_with(const BlockTable& other) const noexcept {
@@ -56,6 +61,16 @@ private:
 
 inline PhysicalBlockID BlockTable::physical_id(std::size_t logical_block) const {
     return pool_->id(entries_.at(logical_block));  // generation-checked
+}
+
+inline void BlockTable::copy_ids(PhysicalBlockID* out) const {
+    constexpr std::size_t kAhead = 16;
+    const std::size_t n = entries_.size();
+    for (std::size_t j = 0; j < n && j < kAhead; ++j) pool_->prefetch(entries_[j]);
+    for (std::size_t j = 0; j < n; ++j) {
+        if (j + kAhead < n) pool_->prefetch(entries_[j + kAhead]);
+        out[j] = pool_->id(entries_[j]);  // generation-checked
+    }
 }
 
 } // namespace kvflux::v2

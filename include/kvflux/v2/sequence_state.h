@@ -48,6 +48,9 @@ public:
     TokenLocation append_token_with_copy(const BlockCopier& copy);
 
     PhysicalBlockID physical_block_id(std::size_t logical_block) const;
+    // out[j] = physical_block_id(j) for j < num_allocated_blocks(), in one
+    // pass (BlockTable::copy_ids).
+    void copy_physical_block_ids(PhysicalBlockID* out) const { table_.copy_ids(out); }
     TokenLocation token_location(std::size_t token_index) const;
 
 private:

@@ -103,9 +103,10 @@ int kvfx_copy_page(const kvfx_cache* cache, uint64_t src_block, uint64_t dst_blo
  *   seq_lens     : device uint64[batch], each in [1, max_seq_len]
  *   max_seq_len  : host-side upper bound of seq_lens (sizes the grid)
  *   pages_per_split: split-K chunk in pages; 0 chooses one from the shape
- *   workspace    : device scratch of kvfx_decode_workspace_bytes(...) bytes,
- *                  zero-filled before its first use and left reusable
- *                  (the kernels reset what they use).
+ *   workspace    : device scratch of kvfx_decode_workspace_bytes(...) bytes;
+ *                  any contents (each launch clears the split counters it
+ *                  uses on `stream` before the kernel), reusable for any
+ *                  shape once the launch that used it has completed.
  * q_heads must be a multiple of num_kv_heads; Q head j uses KV head
  * j / (q_heads / num_kv_heads). Scale 1/sqrt(head_size).
  * Replaces paged_attention_batch's launch (KVFlux src/v2/paged_attention.cu:248-313).

@@ -37,9 +37,7 @@ BatchBlockTable build_batch_block_table(const std::vector<const SequenceState*>&
     out.max_blocks_per_sequence_ = widest;
     out.block_table_.assign(sequences.size() * widest, BatchBlockTable::invalid_block());
     for (std::size_t r = 0; r < sequences.size(); ++r) {
-        PhysicalBlockID* row = out.block_table_.data() + r * widest;
-        const std::size_t n = sequences[r]->num_allocated_blocks();
-        for (std::size_t j = 0; j < n; ++j) row[j] = sequences[r]->physical_block_id(j);
+        sequences[r]->copy_physical_block_ids(out.block_table_.data() + r * widest);
     }
     return out;
 }

@@ -4,11 +4,8 @@
 namespace kvflux::v2 {
 
 ReadBlockTable build_read_block_table(const SequenceState& sequence) {
-    ReadBlockTable ids;
-    ids.reserve(sequence.num_allocated_blocks());
-    for (std::size_t j = 0; j < sequence.num_allocated_blocks(); ++j) {
-        ids.push_back(sequence.physical_block_id(j));
-    }
+    ReadBlockTable ids(sequence.num_allocated_blocks());
+    sequence.copy_physical_block_ids(ids.data());
     return ids;
 }
 

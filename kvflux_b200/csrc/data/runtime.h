@@ -73,7 +73,19 @@ struct StorageRuntime {
     // device addresses of each; push() issues the one H2D copy.
     void stage(const std::size_t* bytes, int n, void** host_out, void** device_out);
     void push();
+    // Copies bytes [offset, offset + bytes) of the staging to the same range
+    // of the device scratch on `stream`.
+    void push_range(std::size_t offset, std::size_t bytes, cudaStream_t stream);
     std::size_t staged_bytes = 0;
+    // A non-blocking stream for uploads and kernels that overlap the kernels
+    // of the default stream, with two events: `side_ready` (recorded on the
+    // default stream) orders the side stream after the caller's earlier work,
+    // `side_done` (recorded on the side stream) orders the default stream
+    // after the side stream's work. Created on first use.
+    void ensure_side();
+    cudaStream_t side = nullptr;
+    cudaEvent_t side_ready = nullptr;
+    cudaEvent_t side_done = nullptr;
     void* ensure_workspace(std::size_t bytes);
     // Synchronises the legacy default stream and raises on device-side flags.
     void finish(const char* op) const;

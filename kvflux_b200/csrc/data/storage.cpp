@@ -60,6 +60,9 @@ StorageRuntime::~StorageRuntime() {
     if (dev_scratch) (void)cudaFree(dev_scratch);
     if (workspace) (void)cudaFree(workspace);
     if (pinned) (void)cudaFreeHost(pinned);
+    if (side_ready) (void)cudaEventDestroy(side_ready);
+    if (side_done) (void)cudaEventDestroy(side_done);
+    if (side) (void)cudaStreamDestroy(side);
     (void)cudaSetDevice(prev);
 }
 
@@ -98,6 +101,24 @@ void StorageRuntime::push() {
     // synchronised the stream, so one buffer suffices.
     cuda_check(cudaMemcpyAsync(dev_scratch, pinned, staged_bytes, cudaMemcpyHostToDevice, nullptr),
                "upload tables");
+}
+
+void StorageRuntime::push_range(std::size_t offset, std::size_t bytes, cudaStream_t stream) {
+    if (bytes == 0) return;
+    cuda_check(cudaMemcpyAsync(static_cast<unsigned char*>(dev_scratch) + offset,
+                               static_cast<const unsigned char*>(pinned) + offset, bytes, cudaMemcpyHostToDevice,
+                               stream),
+               "upload tables");
+}
+
+void StorageRuntime::ensure_side() {
+    if (side == nullptr) cuda_check(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking), "create side stream");
+    if (side_ready == nullptr) {
+        cuda_check(cudaEventCreateWithFlags(&side_ready, cudaEventDisableTiming), "create side event");
+    }
+    if (side_done == nullptr) {
+        cuda_check(cudaEventCreateWithFlags(&side_done, cudaEventDisableTiming), "create side event");
+    }
 }
 
 void StorageRuntime::upload(const void* const* host, const std::size_t* bytes, int n, void** device_out) {

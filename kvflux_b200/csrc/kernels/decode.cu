@@ -23,8 +23,8 @@
 //
 // Split merge: a split writes (max, sum, unnormalised O) to the workspace and
 // bumps a per-(request, head) counter; the CTA that completes the count merges
-// all splits with log-sum-exp weights, writes O and resets the counter. No
-// CTA ever waits for another.
+// all splits with log-sum-exp weights and writes O. The counters are cleared
+// on the stream before each launch. No CTA ever waits for another.
 #include <algorithm>
 #include <cmath>
 
@@ -358,7 +358,6 @@ decode_mma_kernel(const __grid_constant__ DecodeParams p, const __grid_constant_
         }
         p.o[(r * p.kv_heads * G + static_cast<uint64_t>(kh) * G + gg) * HD + d] = acc * s_inv[gg];
     }
-    if (tid == 0) p.counters[pair] = 0u;  // ready for the next launch
 }
 
 bool fast_path(const CacheView& c, uint32_t group) {
@@ -396,6 +395,13 @@ cudaError_t launch_fast(const CacheView& c, const DecodeArgs& a, const CacheMaps
         ((a.batch * c.heads * max_splits * static_cast<uint64_t>(Sh::kPartial) * 4) + 255) & ~uint64_t(255);
     p.counters = reinterpret_cast<unsigned*>(static_cast<char*>(a.workspace) + pbytes);
     p.status = status;
+    if (max_splits > 1) {
+        // The split counters start at zero on the launch's stream. Their
+        // offset follows (batch, max_splits), so in a workspace reused with
+        // another shape they lie where earlier partials were written.
+        const cudaError_t e = cudaMemsetAsync(p.counters, 0, a.batch * c.heads * sizeof(unsigned), s);
+        if (e != cudaSuccess) return e;
+    }
     dim3 grid(max_splits, c.heads, static_cast<uint32_t>(a.batch));
     decode_mma_kernel<HD, T><<<grid, kWarps * 32, Sh::kSmem, s>>>(p, maps->k, maps->v);
     return cudaGetLastError();
@@ -455,13 +461,6 @@ cudaError_t launch_decode(const CacheView& c, const DecodeArgs& a, unsigned* sta
     }
     return c.dtype == KVFX_BF16 ? launch_fast<64, __nv_bfloat16>(c, a, maps, pps, max_splits, status, s)
                                 : launch_fast<64, __half>(c, a, maps, pps, max_splits, status, s);
-}
-
-uint64_t decode_counters_offset(const CacheView& c, uint64_t batch, uint64_t max_len, uint32_t pages_per_split) {
-    const uint32_t pps = clamp_pps(c, max_len, pages_per_split);
-    const uint64_t max_splits = ceil_div(ceil_div(std::max<uint64_t>(max_len, 1), c.bs), pps);
-    const uint64_t per = 8ull * (c.hd + 2);
-    return ((batch * c.heads * max_splits * per * 4) + 255) & ~uint64_t(255);
 }
 
 cudaError_t launch_decode_with_maps(const CacheView& c, const DecodeArgs& a, const CacheMaps& maps,

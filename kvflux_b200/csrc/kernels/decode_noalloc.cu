@@ -158,12 +158,8 @@ extern "C" int kvfx_decode_noalloc(const kvfx_cache* cache, const float* q, floa
     }
     a.workspace = scratch;
     a.workspace_bytes = kNoAllocScratchBytes;
-    // The split counters must start at zero (the array keeps the last call's contents).
-    const uint64_t off = decode_counters_offset(c, batch, max_seq_len, a.pages_per_split);
-    e = cudaMemsetAsync(static_cast<char*>(scratch) + off, 0, counters, s);
-    if (e != cudaSuccess) {
-        return fail(KVFX_ECUDA, std::string("kvfx_decode_noalloc: clear counters: ") + cudaGetErrorString(e));
-    }
+    // The launch clears the split counters it uses on the stream (the array
+    // keeps the last call's contents).
     CacheMaps maps;
     if (!encode_cache_maps(c, &maps, &e)) {
         return fail(KVFX_ECUDA, std::string("kvfx_decode_noalloc: tensor maps: ") + cudaGetErrorString(e));

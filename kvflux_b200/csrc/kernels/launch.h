@@ -111,8 +111,6 @@ const CacheMaps* cache_maps(const CacheView& c, cudaError_t* err);
 // Encodes the maps into caller storage (no caching, no heap allocation).
 bool encode_cache_maps(const CacheView& c, CacheMaps* out, cudaError_t* err);
 
-// Byte offset of the split counters inside a decode workspace.
-uint64_t decode_counters_offset(const CacheView& c, uint64_t batch, uint64_t max_len, uint32_t pages_per_split);
 // The batch-decode fast path with caller-provided tensor maps (16-bit caches,
 // head_size 64/128, block 16, group <= 8 only).
 cudaError_t launch_decode_with_maps(const CacheView& c, const DecodeArgs& a, const CacheMaps& maps,

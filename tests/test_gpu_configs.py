@@ -72,6 +72,51 @@ def test_config3_api_matches_capi(cuda):
     assert kv.device_status(0) == 0
 
 
+def test_config3_api_waits_for_callers_upload(cuda):
+    """The API's second chunk runs on its own stream; it must still see the Q
+    that the caller uploaded on the default stream just before the call, even
+    when that upload is held back (a ~1 ms spin queued ahead of it)."""
+    wl = bench.Decode(kv, w, w.CONFIG3, 0, 1)
+    wl.launch(None)
+    torch.cuda.synchronize()
+    ref = wl.o.clone()
+    q_host = wl.q.cpu().pin_memory()
+    wl.q.zero_()
+    wl.o.fill_(12345.0)
+    torch.cuda.synchronize()
+    torch.cuda._sleep(2_000_000)
+    wl.q.copy_(q_host, non_blocking=True)
+    kv.paged_attention_batch(wl.storage, wl.b.sequences, wl.q, wl.o, wl.qh)
+    torch.cuda.synchronize()
+    assert torch.equal(wl.o, ref)
+    assert kv.device_status(0) == 0
+
+
+def test_api_workspace_reused_across_shapes(cuda):
+    """Two paged_attention_batch calls on one storage: 16 rows of 4096 tokens
+    (every (request, head, split) partial written), then 3 of those rows. The
+    second call's split counters lie where the first call's partials are: it
+    is right only if each launch starts from cleared counters."""
+    cfg = dict(batch=16, q_heads=32, kv_heads=8, head_size=128, block_size=16, min_len=4096, max_len=4096,
+               dtype="bfloat16", seed=0xC0F6)
+    wl = bench.Decode(kv, w, cfg, 0, 1)
+    seqs = wl.b.sequences
+    kv.paged_attention_batch(wl.storage, seqs, wl.q, wl.o, wl.qh)
+    torch.cuda.synchronize()
+    pick = [2, 9, 15]
+    q2 = wl.q.view(wl.batch, -1)[pick].contiguous().view(-1)
+    o2 = torch.full_like(q2, float("nan"))
+    kv.paged_attention_batch(wl.storage, [seqs[i] for i in pick], q2, o2, wl.qh)
+    torch.cuda.synchronize()
+    hk, hv, nb, table, lens, q, o_first = wl.host_sample(pick)
+    exp = oracle.decode_batch(hk, hv, 1, nb, wl.kvh, wl.bs, wl.hd, table, lens, wl.qh, q, threads=16)
+    got = o2.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert float(np.abs(got - exp).max()) < 2e-3
+    assert float(np.abs(o_first - exp).max()) < 2e-3
+    assert kv.device_status(0) == 0
+
+
 def test_config5_decode_sampled_rows(cuda):
     wl = bench.Decode(kv, w, w.CONFIG5, 0, 1)
     lens = wl.lens
