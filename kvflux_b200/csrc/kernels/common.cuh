@@ -111,6 +111,17 @@ __device__ __forceinline__ bool mbar_wait_lean(uint64_t* bar, uint32_t phase, un
     return mbar_wait_slow(a, phase, status);
 }
 
+// True in exactly one lane of a converged warp (PTX elect.sync): code that
+// one thread must issue (tensor-core MMAs, commits) runs under it while the
+// whole warp computes its operands, which stay warp-uniform.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t is = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(is));
+    return is != 0;
+}
+
 // ---------------------------------------------------------- bulk copies ---
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes % 16 == 0,

@@ -245,7 +245,14 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
         if (lane == 0) produce(p, &vmap, smem + kOffV, v_full, pv_done, npages, kVStages);
     } else if (warp == 1) {
         // ----------------------------------------------------- MMA issuer ---
-        if (lane == 0) {
+        // The whole warp runs the schedule (its values stay warp-uniform);
+        // one elected lane issues the MMAs and commits. Waits are voted so
+        // that every lane takes the same path.
+        {
+            const bool leader = elect_one();
+            auto wait = [&](uint64_t* bar, uint32_t phase) {
+                return __all_sync(0xffffffffu, mbar_wait_lean(bar, phase, p.status)) != 0;
+            };
             constexpr bool kBF = std::is_same<T, __nv_bfloat16>::value;
             const uint32_t id_qk = tc::idesc_f16(kBM, kBN, kBF, false);
             const uint32_t id_pv = tc::idesc_f16(kBM, kHD, kBF, true);
@@ -264,9 +271,9 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
             // tensor pipe still has this step's last MMAs queued.
             auto qk_wait = [&]() -> bool {
                 const uint32_t g = qk.g;
-                if (qk.j == 0 && !mbar_wait_lean(&q_full, qk.k & 1u, p.status)) return false;
-                if (!mbar_wait_lean(&k_full[g % kKStages], (g / kKStages) & 1u, p.status)) return false;
-                if (g >= kSBufs && !mbar_wait_lean(&pv_done[g % kSBufs], ((g / kSBufs) - 1) & 1u, p.status))
+                if (qk.j == 0 && !wait(&q_full, qk.k & 1u)) return false;
+                if (!wait(&k_full[g % kKStages], (g / kKStages) & 1u)) return false;
+                if (g >= kSBufs && !wait(&pv_done[g % kSBufs], ((g / kSBufs) - 1) & 1u))
                     return false;
                 tc::fence_after_sync();
                 return true;
@@ -283,21 +290,23 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
                     const uint32_t part = i >> 3, kk = i & 7;
                     const uint32_t a_off = part * kQBytes + (kk >> 2) * kQAtom + (kk & 3) * 32;
                     const uint32_t b_off = (kk >> 2) * kKVHalf + (kk & 3) * 32;
-                    tc::mma(d, q_desc0 + (a_off >> 4), k_desc + (b_off >> 4), id_qk, i > 0 ? 1u : 0u);
+                    if (leader) tc::mma(d, q_desc0 + (a_off >> 4), k_desc + (b_off >> 4), id_qk, i > 0 ? 1u : 0u);
                 }
             };
             auto qk_finish = [&]() {
-                tc::commit(&s_full[qk.g % kSBufs]);
-                if (qk.last()) tc::commit(&q_free);  // Q may be replaced once this completes
+                if (leader) {
+                    tc::commit(&s_full[qk.g % kSBufs]);
+                    if (qk.last()) tc::commit(&q_free);
+                }  // Q may be replaced once this completes
                 qk.next(p);
             };
             // O += P(g) V_g with P from TMEM; a unit's first PV overwrites O,
             // which the previous unit's epilogue must have read.
             auto pv_wait = [&]() -> bool {
                 const uint32_t g = pv.g;
-                if (pv.j == 0 && pv.k >= 1 && !mbar_wait_lean(&o_free, (pv.k - 1) & 1u, p.status)) return false;
-                if (!mbar_wait_lean(&v_full[g % kVStages], (g / kVStages) & 1u, p.status)) return false;
-                if (!mbar_wait_lean(&p_full[g % kSBufs], (g / kSBufs) & 1u, p.status)) return false;
+                if (pv.j == 0 && pv.k >= 1 && !wait(&o_free, (pv.k - 1) & 1u)) return false;
+                if (!wait(&v_full[g % kVStages], (g / kVStages) & 1u)) return false;
+                if (!wait(&p_full[g % kSBufs], (g / kSBufs) & 1u)) return false;
                 tc::fence_after_sync();
                 return true;
             };
@@ -311,12 +320,15 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
                     if (i < from || i >= to) continue;
                     const uint32_t t = i >> 1, part = i & 1;
                     const uint32_t a = pt + (t >> 1) * 32 + part * 16 + (t & 1) * 8;
-                    tc::mma_ts(tmem + kTmemO, a, v_desc + ((t * 2048) >> 4), id_pv, (pv.j > 0 || i > 0) ? 1u : 0u);
+                    if (leader)
+                        tc::mma_ts(tmem + kTmemO, a, v_desc + ((t * 2048) >> 4), id_pv, (pv.j > 0 || i > 0) ? 1u : 0u);
                 }
             };
             auto pv_finish = [&]() {
-                tc::commit(&pv_done[pv.g % kSBufs]);
-                if (pv.last()) tc::commit(&o_full);
+                if (leader) {
+                    tc::commit(&pv_done[pv.g % kSBufs]);
+                    if (pv.last()) tc::commit(&o_full);
+                }
                 pv.next(p);
             };
             constexpr uint32_t kSplit = 12;  // MMAs of a step issued before the next step's waits
@@ -338,17 +350,19 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
                 pv_finish();
                 if (!ok) break;
                 if (more_qk) {
-                    qk_mmas(0, kSplit);
-                    if (pv.valid) ok = pv_wait();
-                    qk_mmas(kSplit, 16);
+                    // All of QK(g + 2) and its commit before the wait for
+                    // P(g + 1): the softmax of tile g + 2 starts as soon as
+                    // it is done with g + 1, and 16 queued MMAs cover the wait.
+                    qk_mmas(0, 16);
                     qk_finish();
+                    if (pv.valid) ok = pv_wait();
                 } else if (pv.valid) {
                     ok = pv_wait();
                 }
             }
             // Every MMA this thread issued is complete before TMEM is released.
-            tc::commit(&mma_done);
-            (void)mbar_wait_lean(&mma_done, 0, p.status);
+            if (leader) tc::commit(&mma_done);
+            (void)wait(&mma_done, 0);
         }
     } else if (warp >= 4 && warp < 8) {
         // -------------------------------------------------------- softmax ---
