@@ -139,18 +139,22 @@ __device__ __forceinline__ uint32_t swz_row(uint32_t r, uint32_t c) {
     return (r >> 3) * 1024 + (r & 7) * 128 + (((c ^ r) & 7) << 4);
 }
 
-// Page ids of KV tile j (8 pages), loaded together: one memory round trip.
-__device__ __forceinline__ void tile_pages(const PrefillParams& p, uint32_t j, uint64_t npages, uint64_t* ids) {
-#pragma unroll
-    for (int pg = 0; pg < kBN / 16; ++pg) {
-        const uint64_t lp = static_cast<uint64_t>(j) * (kBN / 16) + pg;
-        ids[pg] = __ldg(p.blocks + (lp < npages ? lp : 0));
-    }
+// Page id of page `lane` of KV tile j in lanes 0..7 (one load per lane, all
+// in one memory round trip); 0 in the other lanes.
+__device__ __forceinline__ uint64_t tile_page_id(const PrefillParams& p, uint32_t j, uint64_t npages, uint32_t lane) {
+    if (lane >= kBN / 16) return 0;
+    const uint64_t lp = static_cast<uint64_t>(j) * (kBN / 16) + lane;
+    return __ldg(p.blocks + (lp < npages ? lp : 0));
 }
 
-// One KV tile (8 pages of one KV head) into a ring slot.
+// One KV tile (8 pages of one KV head) into a ring slot. Warp-wide: page pg's
+// id comes from lane pg; the elected lane issues the 16 copies.
 __device__ __forceinline__ void load_kv_tile(const PrefillParams& p, const CUtensorMap* map, unsigned char* dst,
-                                             uint32_t kh, const uint64_t* ids, uint64_t* bar) {
+                                             uint32_t kh, uint64_t lane_id, bool leader, uint64_t* bar) {
+    uint64_t ids[kBN / 16];
+#pragma unroll
+    for (int pg = 0; pg < kBN / 16; ++pg) ids[pg] = __shfl_sync(0xffffffffu, lane_id, pg);
+    if (!leader) return;
     mbar_arrive_expect_tx(bar, kKVTile);
 #pragma unroll
     for (int pg = 0; pg < kBN / 16; ++pg) {
@@ -167,34 +171,39 @@ __device__ __forceinline__ void load_kv_tile(const PrefillParams& p, const CUten
     }
 }
 
-// Producer loop of one ring (K or V) of `kStages` slots: before tile g is
+// Producer loop of one ring (K or V) of `kStages` slots, run by a whole warp
+// (voted waits, one elected lane issuing the copies): before tile g is
 // loaded into slot g % kStages, the MMA that read tile g - kStages must have
-// completed, which the MMA thread's commit to done[(g - kStages) % kSBufs]
+// completed, which the MMA warp's commit to done[(g - kStages) % kSBufs]
 // signals (s_full for K: QK(g) completes; pv_done for V: PV(g) completes).
 // Neither barrier can run a phase ahead: tile g's own MMA needs this load.
 // The next tile's page ids are fetched while waiting for its slot. At the
 // end, waits for its own copies in flight.
 __device__ __noinline__ void produce(const PrefillParams& p, const CUtensorMap* map, unsigned char* ring,
                                      uint64_t* full, uint64_t* done, uint64_t npages, uint32_t kStages) {
-    prefetch_tensormap(map);
+    const uint32_t lane = threadIdx.x & 31u;
+    const bool leader = elect_one();
+    auto wait = [&](uint64_t* bar, uint32_t phase) {
+        return __all_sync(0xffffffffu, mbar_wait_lean(bar, phase, p.status)) != 0;
+    };
+    if (leader) prefetch_tensormap(map);
     TileCursor c;
     c.init(p);
-    uint64_t ids[kBN / 16];
-    if (c.valid) tile_pages(p, c.j, npages, ids);
+    uint64_t id = c.valid ? tile_page_id(p, c.j, npages, lane) : 0;
     uint32_t issued = 0;
     while (c.valid) {
         const uint32_t g = c.g, st = g % kStages;
         if (g >= kStages) {
             const uint32_t prev = g - kStages;
-            if (!mbar_wait_lean(&done[prev % kSBufs], (prev / kSBufs) & 1u, p.status)) break;
+            if (!wait(&done[prev % kSBufs], (prev / kSBufs) & 1u)) break;
         }
-        load_kv_tile(p, map, ring + st * kKVTile, c.u.kh, ids, &full[st]);
+        load_kv_tile(p, map, ring + st * kKVTile, c.u.kh, id, leader, &full[st]);
         issued = g + 1;
         c.next(p);
-        if (c.valid) tile_pages(p, c.j, npages, ids);
+        if (c.valid) id = tile_page_id(p, c.j, npages, lane);
     }
     for (uint32_t g = issued > kStages ? issued - kStages : 0; g < issued; ++g)
-        (void)mbar_wait_lean(&full[g % kStages], (g / kStages) & 1u, p.status);
+        (void)wait(&full[g % kStages], (g / kStages) & 1u);
 }
 
 template <typename T>
@@ -239,10 +248,10 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
 
     if (warp == 0) {
         // ---------------------------------------------------- K producer ---
-        if (lane == 0) produce(p, &kmap, smem + kOffK, k_full, s_full, npages, kKStages);
+        produce(p, &kmap, smem + kOffK, k_full, s_full, npages, kKStages);
     } else if (warp == 2) {
         // ---------------------------------------------------- V producer ---
-        if (lane == 0) produce(p, &vmap, smem + kOffV, v_full, pv_done, npages, kVStages);
+        produce(p, &vmap, smem + kOffV, v_full, pv_done, npages, kVStages);
     } else if (warp == 1) {
         // ----------------------------------------------------- MMA issuer ---
         // The whole warp runs the schedule (its values stay warp-uniform);
@@ -252,6 +261,15 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
             const bool leader = elect_one();
             auto wait = [&](uint64_t* bar, uint32_t phase) {
                 return __all_sync(0xffffffffu, mbar_wait_lean(bar, phase, p.status)) != 0;
+            };
+            // Two barriers at once: both try_waits issue back to back and
+            // one vote covers them (both are usually complete already); the
+            // bounded slow path runs only when one is not.
+            auto wait2 = [&](uint64_t* a, uint32_t pa, uint64_t* b, uint32_t pb) {
+                const bool fa = mbar_try_wait(smem_addr(a), pa);
+                const bool fb = mbar_try_wait(smem_addr(b), pb);
+                if (__all_sync(0xffffffffu, fa && fb)) return true;
+                return wait(a, pa) && wait(b, pb);
             };
             constexpr bool kBF = std::is_same<T, __nv_bfloat16>::value;
             const uint32_t id_qk = tc::idesc_f16(kBM, kBN, kBF, false);
@@ -272,9 +290,13 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
             auto qk_wait = [&]() -> bool {
                 const uint32_t g = qk.g;
                 if (qk.j == 0 && !wait(&q_full, qk.k & 1u)) return false;
-                if (!wait(&k_full[g % kKStages], (g / kKStages) & 1u)) return false;
-                if (g >= kSBufs && !wait(&pv_done[g % kSBufs], ((g / kSBufs) - 1) & 1u))
+                if (g >= kSBufs) {
+                    if (!wait2(&k_full[g % kKStages], (g / kKStages) & 1u, &pv_done[g % kSBufs],
+                               ((g / kSBufs) - 1) & 1u))
+                        return false;
+                } else if (!wait(&k_full[g % kKStages], (g / kKStages) & 1u)) {
                     return false;
+                }
                 tc::fence_after_sync();
                 return true;
             };
@@ -305,8 +327,8 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
             auto pv_wait = [&]() -> bool {
                 const uint32_t g = pv.g;
                 if (pv.j == 0 && pv.k >= 1 && !wait(&o_free, (pv.k - 1) & 1u)) return false;
-                if (!wait(&v_full[g % kVStages], (g / kVStages) & 1u)) return false;
-                if (!wait(&p_full[g % kSBufs], (g / kSBufs) & 1u)) return false;
+                if (!wait2(&v_full[g % kVStages], (g / kVStages) & 1u, &p_full[g % kSBufs], (g / kSBufs) & 1u))
+                    return false;
                 tc::fence_after_sync();
                 return true;
             };
