@@ -335,6 +335,100 @@ def e2e_decode(kv, wl: Decode, steps: int, warmup: int):
     return ms, q_host.numel() * 4 + table_bytes, o_host.numel() * 4
 
 
+def decode_step(kv, wl: Decode, steps: int, warmup: int, ranks: Ranks) -> dict:
+    """Config 5 as a serving decode step: every sequence appends one token.
+
+    e2e: BatchDecodeSession.step (host page bookkeeping with copy-on-write,
+    16 bytes per row of lengths and slots uploaded, one fused write + decode
+    launch over the device-resident block table), with the step's new K/V
+    rows and Q copied from pinned host memory and O copied back, all inside
+    the timed region. Device: the fused launch alone, repeated on the state
+    after the last step (it rewrites the same rows), next to a plain decode
+    launch over the same table and lengths."""
+    import torch
+
+    seqs = wl.b.sequences
+    # The pool holds exactly the prefilled pages; hand back enough held pages
+    # for the steps' new pages (at most one per sequence per step).
+    spare = min(len(wl.b.holders), 2 * wl.batch)
+    for h in wl.b.holders[:spare]:
+        wl.b.pool.free(h)
+    del wl.b.holders[:spare]
+    n = wl.batch * wl.kvh * wl.hd
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(wl.cfg["seed"] * 11 + ranks.rank)
+    k_dev = torch.randn(n, generator=gen, device="cuda").to(torch.bfloat16)
+    v_dev = torch.randn(n, generator=gen, device="cuda").to(torch.bfloat16)
+    k_host, v_host = k_dev.cpu().pin_memory(), v_dev.cpu().pin_memory()
+    q_host = wl.q.cpu().pin_memory()
+    o_host = torch.empty_like(q_host).pin_memory()
+    sess = kv.BatchDecodeSession(wl.storage, seqs, wl.qh)
+
+    def step():
+        k_dev.copy_(k_host, non_blocking=True)
+        v_dev.copy_(v_host, non_blocking=True)
+        wl.q.copy_(q_host, non_blocking=True)
+        sess.step(k_dev, v_dev, wl.q, wl.o)
+        o_host.copy_(wl.o, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    ranks.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall = time.perf_counter()
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall
+    e2e_ms = max(t0.elapsed_time(t1), wall * 1e3) / steps
+    ranks.barrier()
+
+    lens = np.array([s.num_tokens() for s in seqs], np.uint64)
+    slots = np.array(kv.build_slot_mapping([(s, s.num_tokens() - 1) for s in seqs]), np.uint64)
+    lens_d = torch.from_numpy(lens.view(np.int64)).cuda()
+    slots_d = torch.from_numpy(slots.view(np.int64)).cuda()
+    width, table = sess.table_width(), sess.device_table()
+    max_len = int(lens.max())
+    pps = kv.lib.kvfx_decode_pages_per_split(ctypes.byref(wl.desc), wl.batch, wl.qh, max_len, int(lens.sum()))
+    ws_bytes = kv.lib.kvfx_decode_workspace_bytes(ctypes.byref(wl.desc), wl.batch, wl.qh, max_len, pps)
+    ws = torch.zeros(max(int(ws_bytes), 16), dtype=torch.uint8, device="cuda")
+
+    def fused(stream):
+        kv.check(kv.lib.kvfx_decode_append(ctypes.byref(wl.desc), k_dev.data_ptr(), v_dev.data_ptr(),
+                                           slots_d.data_ptr(), wl.q.data_ptr(), wl.o.data_ptr(), table,
+                                           lens_d.data_ptr(), wl.batch, width, wl.qh, max_len, pps, ws.data_ptr(),
+                                           ws.numel(), stream), "kvfx_decode_append")
+
+    def plain(stream):
+        kv.check(kv.lib.kvfx_decode(ctypes.byref(wl.desc), wl.q.data_ptr(), wl.o.data_ptr(), table,
+                                    lens_d.data_ptr(), wl.batch, width, wl.qh, max_len, pps, ws.data_ptr(),
+                                    ws.numel(), stream), "kvfx_decode")
+
+    _, tot_f = time_launches(fused, steps, warmup, ranks)
+    _, tot_p = time_launches(plain, steps, warmup, ranks)
+    if kv.device_status(torch.cuda.current_device()) != 0:
+        raise RuntimeError("decode step: a kernel flagged an out-of-range id or a timed-out wait")
+    fused_ms = ranks.reduce(tot_f / steps, "max")
+    plain_ms = ranks.reduce(tot_p / steps, "max")
+    e2e_ms = ranks.reduce(e2e_ms, "max")
+    kv_bytes = ranks.reduce(float(int(lens.sum()) * wl.kvh * wl.hd * 2 * 2), "sum")
+    tokens = wl.batch
+    world = ranks.world
+    return {"workload": "config5 decode step: 256 sequences append one token each (copy-on-write, new pages), "
+                        "fused KV write + decode over a device-resident block table",
+            "e2e_ms_per_step": e2e_ms, "e2e_tokens_per_s": tokens / (e2e_ms * 1e-3),
+            "e2e_kv_gbs": kv_bytes / (e2e_ms * 1e-3) / 1e9,
+            "e2e_h2d_bytes_per_step": world * (2 * k_host.numel() * 2 + q_host.numel() * 4 + 2 * tokens * 8),
+            "e2e_d2h_bytes_per_step": world * o_host.numel() * 4,
+            "api": "kvflux::v2::BatchDecodeSession::step",
+            "fused_ms_per_launch": fused_ms, "fused_kv_gbs": kv_bytes / (fused_ms * 1e-3) / 1e9,
+            "plain_decode_ms_per_launch": plain_ms, "table_width": width}
+
+
 class WriteGather:
     """Config 2 on one rank's KV-head shard."""
 
@@ -610,6 +704,13 @@ def only_case(args, ranks: Ranks, kv, w, peak: float) -> int:
         out = {"case": args.only, "batch": cfg["batch"], "ms_per_launch": ms, "kv_bytes": wl.kv_bytes,
                "algorithmic_bytes": wl.alg_bytes, "gbs": wl.alg_bytes / (ms * 1e-3) / 1e9,
                "pages_per_split": wl.pps}
+    elif args.only == "step5":
+        cfg = dict(w.CONFIG5)
+        if args.batch:
+            cfg["batch"] = args.batch
+        wl = Decode(kv, w, cfg, ranks.rank, ranks.world)
+        out = decode_step(kv, wl, args.steps, args.warmup, ranks)
+        out.update({"case": args.only, "batch": cfg["batch"], "gbs": out["fused_kv_gbs"]})
     elif args.only == "prefill4":
         pf = Prefill(kv, w, w.CONFIG4)
         per, total = time_launches(pf.launch, args.steps, args.warmup, ranks)
@@ -647,7 +748,7 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="headline decode only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather", "prefill4"],
+    ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather", "prefill4", "step5"],
                     help="run one kernel's case alone (profiling runs); prints a short JSON line")
     ap.add_argument("--batch", type=int, default=None, help="override the batch: decode requests, write/gather sequences (profiling runs)")
     args = ap.parse_args(argv)
@@ -712,6 +813,8 @@ def main(argv=None) -> int:
 
     secondary = {}
     if not args.no_secondary:
+        # Mutates the sequences (one token per step) and wl.o: after the CPU leg.
+        secondary["decode_step_cfg5"] = decode_step(kv, wl, max(3, args.steps // 2), 3, ranks)
         del wl
         torch.cuda.empty_cache()
         wg = WriteGather(kv, w, w.CONFIG2, rank, world)

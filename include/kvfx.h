@@ -124,6 +124,29 @@ int kvfx_decode(const kvfx_cache* cache, const float* q, float* o,
                 void* stream);
 
 /*
+ * One batch decode step fused with its paged KV write. Row b's new token is
+ * position seq_lens[b] - 1 (seq_lens already count it); its K/V rows are
+ * k_new/v_new[b][num_kv_heads][head_size] in the cache dtype and its slot is
+ * new_slots[b] (device uint64[batch]), whose offset in its page must equal
+ * (seq_lens[b] - 1) % block_size. The launch writes those rows into the cache,
+ * stores the slot's page into block_table[b][(seq_lens[b] - 1) / block_size]
+ * (block_table is device memory that stays resident between steps; entries
+ * before that column are read as they are), and computes the same attention
+ * as kvfx_decode over the updated rows; q, o, workspace and the other
+ * arguments as for kvfx_decode. A slot outside the cache or at the wrong
+ * offset is not written and sets KVFX_FLAG_BAD_INDEX.
+ * Replaces, for a batch, the write_paged_kv + paged_attention pair of the
+ * reference's decode step (KVFlux src/v2/sequence_lifecycle.cpp:53-73), with
+ * the block table kept on the device instead of uploaded per call
+ * (src/v2/paged_attention.cu:287-292).
+ */
+int kvfx_decode_append(const kvfx_cache* cache, const void* k_new, const void* v_new,
+                       const uint64_t* new_slots, const float* q, float* o, uint64_t* block_table,
+                       const uint64_t* seq_lens, uint64_t batch, uint64_t max_blocks_per_seq,
+                       uint32_t q_heads, uint64_t max_seq_len, uint32_t pages_per_split,
+                       void* workspace, uint64_t workspace_bytes, void* stream);
+
+/*
  * Batch decode that allocates nothing: the same computation and arguments as
  * kvfx_decode without pages_per_split and the workspace. No counterpart in
  * the reference. For callers that cannot call cudaMalloc: engines that hand

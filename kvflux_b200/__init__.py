@@ -7,7 +7,8 @@ Two native surfaces, both built in-tree by ``python kvflux_b200/build.py``:
 * ``kvflux_b200._C`` (re-exported here) - the reference's C++ v2 API
   (PhysicalBlockPool, SequenceState, PagedKVStorage, write_paged_kv,
   read_paged_kv, paged_attention, paged_attention_batch, append_token_cow,
-  PrefixCache, SequenceLifecycle, ...) running on those kernels.
+  PrefixCache, SequenceLifecycle, ...) running on those kernels, plus
+  BatchDecodeSession (batched decode steps over a device-resident block table).
 
 There is no fallback: importing fails loudly if the extension is not built.
 """
@@ -63,6 +64,7 @@ def _load():
     L.kvfx_decode_pages_per_split.argtypes = [C, u64, u32, u64, u64]
     L.kvfx_decode_pages_per_split.restype = u32
     L.kvfx_decode.argtypes = [C, vp, vp, vp, vp, u64, u64, u32, u64, u32, vp, u64, vp]
+    L.kvfx_decode_append.argtypes = [C, vp, vp, vp, vp, vp, vp, vp, u64, u64, u32, u64, u32, vp, u64, vp]
     L.kvfx_decode_noalloc.argtypes = [C, vp, vp, vp, vp, u64, u64, u32, u64, vp]
     L.kvfx_attention_workspace_bytes.argtypes = [C, u64, u64, u32]
     L.kvfx_attention_workspace_bytes.restype = u64
@@ -80,7 +82,7 @@ lib = _load()
 #: Every symbol include/kvfx.h declares (checked by the tests).
 KVFX_SYMBOLS = (
     "kvfx_write", "kvfx_gather", "kvfx_gather_batch", "kvfx_copy_page", "kvfx_decode_workspace_bytes",
-    "kvfx_decode_pages_per_split", "kvfx_decode", "kvfx_decode_noalloc", "kvfx_attention_workspace_bytes",
+    "kvfx_decode_pages_per_split", "kvfx_decode", "kvfx_decode_append", "kvfx_decode_noalloc", "kvfx_attention_workspace_bytes",
     "kvfx_attention",
     "kvfx_last_error", "kvfx_device_status", "kvfx_version",
 )

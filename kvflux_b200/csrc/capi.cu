@@ -259,6 +259,47 @@ int kvfx_decode(const kvfx_cache* cache, const float* q, float* o, const uint64_
     return e == cudaSuccess ? KVFX_OK : cuda_fail("batch decode launch", e);
 }
 
+int kvfx_decode_append(const kvfx_cache* cache, const void* k_new, const void* v_new,
+                       const uint64_t* new_slots, const float* q, float* o, uint64_t* block_table,
+                       const uint64_t* seq_lens, uint64_t batch, uint64_t max_blocks_per_seq,
+                       uint32_t q_heads, uint64_t max_seq_len, uint32_t pages_per_split, void* workspace,
+                       uint64_t workspace_bytes, void* stream) {
+    kvfx::CacheView c;
+    if (int rc = make_view(cache, &c); rc != KVFX_OK) return rc;
+    if (q_heads == 0 || q_heads % c.heads != 0) {
+        return fail(KVFX_EINVAL, "q_heads must be a positive multiple of num_kv_heads");
+    }
+    if (batch == 0) return KVFX_OK;
+    if (k_new == nullptr || v_new == nullptr || new_slots == nullptr || q == nullptr || o == nullptr ||
+        block_table == nullptr || seq_lens == nullptr) {
+        return fail(KVFX_EINVAL, "k_new, v_new, new_slots, q, o, block_table and seq_lens must be non-null");
+    }
+    if (batch > 65535) return fail(KVFX_EINVAL, "batch above 65535 sequences per launch");
+    if (max_seq_len == 0) return fail(KVFX_EINVAL, "max_seq_len must be positive");
+    if (max_blocks_per_seq < kvfx::ceil_div(max_seq_len, c.bs)) {
+        return fail(KVFX_EINVAL, "max_blocks_per_seq is smaller than max_seq_len needs");
+    }
+    uint64_t elems = 0, tmp = 0;
+    if (!mul_ok(batch, q_heads, &tmp) || !mul_ok(tmp, c.hd, &elems) || !mul_ok(batch, c.heads, &tmp) ||
+        !mul_ok(tmp, c.row_bytes, &elems)) {
+        return fail(KVFX_EOVERFLOW, "query or new-token size overflows");
+    }
+    const uint64_t need = kvfx::decode_workspace_bytes(c, batch, q_heads, max_seq_len, pages_per_split);
+    if (need != 0 && (workspace == nullptr || workspace_bytes < need)) {
+        return fail(KVFX_ENOSPACE, "decode workspace is smaller than kvfx_decode_workspace_bytes()");
+    }
+    DeviceScope scope(c.device);
+    if (scope.error() != cudaSuccess) return cuda_fail("select device", scope.error());
+    kvfx::DecodeArgs a{q, o, block_table, seq_lens, batch, max_blocks_per_seq, max_seq_len,
+                       q_heads, pages_per_split, workspace, workspace_bytes};
+    a.k_new = k_new;
+    a.v_new = v_new;
+    a.new_slots = new_slots;
+    a.table_out = block_table;
+    const cudaError_t e = kvfx::launch_decode(c, a, status_word(c.device), static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? KVFX_OK : cuda_fail("batch decode append launch", e);
+}
+
 uint64_t kvfx_attention_workspace_bytes(const kvfx_cache* cache, uint64_t query_tokens, uint64_t kv_tokens,
                                         uint32_t q_heads) {
     kvfx::CacheView c;

@@ -25,6 +25,12 @@
 // bumps a per-(request, head) counter; the CTA that completes the count merges
 // all splits with log-sum-exp weights and writes O. The counters are cleared
 // on the stream before each launch. No CTA ever waits for another.
+//
+// Append mode (one decode step fused with its paged KV write): each row's new
+// token is the last position; the CTA whose split holds that page writes the
+// new K/V row of its head into the cache, replaces the row in its shared-
+// memory tiles, and takes the page from the token's slot, so the launch needs
+// neither a separate write kernel nor a host update of the table.
 #include <algorithm>
 #include <cmath>
 
@@ -56,6 +62,13 @@ struct DecodeParams {
     float* partial;
     unsigned* counters;
     unsigned* status;
+    // Append mode (all null for a plain decode): see DecodeArgs.
+    const void* k_new;
+    const void* v_new;
+    const uint64_t* new_slots;
+    uint64_t* table_out;
+    char* k_base;
+    char* v_base;
 };
 
 template <int HD>
@@ -108,6 +121,41 @@ decode_mma_kernel(const __grid_constant__ DecodeParams p, const __grid_constant_
         pend > pbeg + warp ? static_cast<uint32_t>(ceil_div(pend - pbeg - warp, kWarps)) : 0u;
     unsigned char* wsm = smem + static_cast<size_t>(warp) * kStages * S::kStage;
 
+    // Append mode: the CTA holding the row's last page writes this head's
+    // new K/V row into the cache and into that page's tiles once they land
+    // (so the TMA load may see the old or the new row: either is replaced),
+    // and loads the page the slot names in place of the table entry. No
+    // other CTA reads that table entry in this launch; the head-0 CTA stores
+    // the page there for later launches.
+    const bool append = p.k_new != nullptr;
+    const uint64_t last = npages - 1;
+    uint64_t new_blk = ~0ull;
+    uint32_t new_row = 0;
+    if (append && split == nsplits - 1) {
+        const uint64_t slot = p.new_slots[r];
+        if ((slot >> 4) < p.num_blocks && (slot & 15u) == ((len - 1) & 15u)) {
+            new_blk = slot >> 4;
+            new_row = static_cast<uint32_t>(slot & 15u);
+        } else if (tid == 0) {
+            raise_flag(p.status, KVFX_FLAG_BAD_INDEX);
+        }
+    }
+    const bool owns_new = new_blk != ~0ull && static_cast<uint32_t>((last - pbeg) % kWarps) == warp;
+    constexpr int kRowChunks = HD / 8;  // 16-byte chunks of one (token, head) row
+    uint4 new_chunk = make_uint4(0, 0, 0, 0);
+    if (owns_new) {
+        if (lane < 2 * kRowChunks) {
+            const bool isv = lane >= kRowChunks;
+            const int c = isv ? lane - kRowChunks : lane;
+            const uint64_t row_off = ((r * p.kv_heads + kh) * HD) * 2 + static_cast<uint64_t>(c) * 16;
+            new_chunk = __ldg(reinterpret_cast<const uint4*>(static_cast<const char*>(isv ? p.v_new : p.k_new) +
+                                                             row_off));
+            const uint64_t dst = (((new_blk * p.kv_heads + kh) * 16 + new_row) * HD) * 2 + static_cast<uint64_t>(c) * 16;
+            *reinterpret_cast<uint4*>((isv ? p.v_base : p.k_base) + dst) = new_chunk;
+        }
+        if (kh == 0 && lane == 0) p.table_out[r * p.max_blocks + last] = new_blk;
+    }
+
     if (lane == 0) {
         for (int st = 0; st < kStages; ++st) mbar_init(&bars[warp][st], 1);
         fence_mbarrier_init();
@@ -119,7 +167,12 @@ decode_mma_kernel(const __grid_constant__ DecodeParams p, const __grid_constant_
     auto issue = [&](uint32_t i) {  // lane 0: load page i of this warp
         if (i >= n_my) return;
         const uint64_t j = pbeg + warp + static_cast<uint64_t>(kWarps) * i;
-        uint64_t blk = __ldg(row + j);
+        uint64_t blk;
+        if (!append) {
+            blk = __ldg(row + j);
+        } else {
+            blk = j == last && new_blk != ~0ull ? new_blk : __ldcg(row + j);
+        }
         if (blk >= p.num_blocks) {
             raise_flag(p.status, KVFX_FLAG_BAD_INDEX);
             blk = 0;
@@ -175,6 +228,15 @@ decode_mma_kernel(const __grid_constant__ DecodeParams p, const __grid_constant_
         const uint32_t kt = smem_addr(ktp), vt = kt + S::kTile;
         const uint64_t tok0 = (pbeg + warp + static_cast<uint64_t>(kWarps) * i) * 16;
         const int valid = static_cast<int>(umin64(16, len - tok0));
+        if (owns_new && tok0 + 16 >= len) {  // this warp's last page holds the new token
+            if (lane < 2 * kRowChunks) {
+                const bool isv = lane >= kRowChunks;
+                const int c = isv ? lane - kRowChunks : lane;
+                *reinterpret_cast<uint4*>(ktp + (isv ? S::kTile : 0u) + swz(static_cast<int>(new_row), c)) =
+                    new_chunk;
+            }
+            __syncwarp();
+        }
         if (valid < 16) {
             // Zero V rows past the sequence end (they may hold anything).
             uint4* vz = reinterpret_cast<uint4*>(ktp + S::kTile);
@@ -360,6 +422,35 @@ decode_mma_kernel(const __grid_constant__ DecodeParams p, const __grid_constant_
     }
 }
 
+// Append step for the shapes the fast kernel does not cover, ahead of the
+// generic attention launch: one CTA per row validates the new token's slot
+// against its position, stores the slot's page into the table and copies the
+// row's K/V for every head (element-wise).
+template <typename E>
+__global__ void append_rows_kernel(char* k, char* v, const void* k_new, const void* v_new,
+                                   const uint64_t* new_slots, uint64_t* table, const uint64_t* lens,
+                                   uint64_t max_blocks, uint64_t num_blocks, uint32_t heads, uint32_t bs,
+                                   uint32_t hd, unsigned* status) {
+    const uint64_t r = blockIdx.x;
+    const uint64_t len = lens[r];
+    const uint64_t slot = new_slots[r];
+    const uint64_t blk = slot / bs, off = slot % bs;
+    if (len == 0 || (len - 1) / bs >= max_blocks || blk >= num_blocks || off != (len - 1) % bs) {
+        if (threadIdx.x == 0) raise_flag(status, KVFX_FLAG_BAD_INDEX);
+        return;
+    }
+    if (threadIdx.x == 0) table[r * max_blocks + (len - 1) / bs] = blk;
+    const uint64_t n = static_cast<uint64_t>(heads) * hd;
+    const E* ks = static_cast<const E*>(k_new) + r * n;
+    const E* vs = static_cast<const E*>(v_new) + r * n;
+    for (uint64_t x = threadIdx.x; x < n; x += blockDim.x) {
+        const uint64_t h = x / hd, d = x - h * hd;
+        const uint64_t dst = ((blk * heads + h) * bs + off) * hd + d;
+        reinterpret_cast<E*>(k)[dst] = ks[x];
+        reinterpret_cast<E*>(v)[dst] = vs[x];
+    }
+}
+
 bool fast_path(const CacheView& c, uint32_t group) {
     return (c.dtype == KVFX_BF16 || c.dtype == KVFX_F16) && c.bs == 16 &&
            (c.hd == 64 || c.hd == 128) && group >= 1 && group <= 8 &&
@@ -395,6 +486,12 @@ cudaError_t launch_fast(const CacheView& c, const DecodeArgs& a, const CacheMaps
         ((a.batch * c.heads * max_splits * static_cast<uint64_t>(Sh::kPartial) * 4) + 255) & ~uint64_t(255);
     p.counters = reinterpret_cast<unsigned*>(static_cast<char*>(a.workspace) + pbytes);
     p.status = status;
+    p.k_new = a.k_new;
+    p.v_new = a.v_new;
+    p.new_slots = a.new_slots;
+    p.table_out = a.table_out;
+    p.k_base = c.k;
+    p.v_base = c.v;
     if (max_splits > 1) {
         // The split counters start at zero on the launch's stream. Their
         // offset follows (batch, max_splits), so in a workspace reused with
@@ -442,7 +539,22 @@ uint64_t decode_workspace_bytes(const CacheView& c, uint64_t batch, uint32_t q_h
 
 cudaError_t launch_decode(const CacheView& c, const DecodeArgs& a, unsigned* status, cudaStream_t s) {
     const uint32_t group = a.q_heads / c.heads;
-    if (!fast_path(c, group)) {
+    const bool append = a.k_new != nullptr;
+    const bool aligned = !append || ((reinterpret_cast<uintptr_t>(a.k_new) | reinterpret_cast<uintptr_t>(a.v_new)) & 15u) == 0;
+    if (!fast_path(c, group) || !aligned) {
+        if (append) {
+            if (c.elem == 4) {
+                append_rows_kernel<uint32_t><<<static_cast<uint32_t>(a.batch), 128, 0, s>>>(
+                    c.k, c.v, a.k_new, a.v_new, a.new_slots, a.table_out, a.lens, a.max_blocks, c.num_blocks,
+                    c.heads, c.bs, c.hd, status);
+            } else {
+                append_rows_kernel<uint16_t><<<static_cast<uint32_t>(a.batch), 128, 0, s>>>(
+                    c.k, c.v, a.k_new, a.v_new, a.new_slots, a.table_out, a.lens, a.max_blocks, c.num_blocks,
+                    c.heads, c.bs, c.hd, status);
+            }
+            const cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess) return e;
+        }
         GenericAttnArgs g{a.q, a.o, a.table, a.max_blocks, a.lens, a.batch, 0, a.q_heads};
         return launch_attention_generic(c, g, status, s);
     }

@@ -62,6 +62,16 @@ struct DecodeArgs {
     uint32_t q_heads, pages_per_split;
     void* workspace;
     uint64_t workspace_bytes;
+    // Append mode (kvfx_decode_append), all null for a plain decode: row b's
+    // new token sits at position lens[b] - 1, its K/V rows are
+    // k_new/v_new[b][h][:] (cache dtype) and its slot is new_slots[b]; the
+    // launch writes them into the cache, stores the slot's page into
+    // table_out[b][(lens[b] - 1) / bs] (table_out == table) and attends over
+    // the updated rows.
+    const void* k_new = nullptr;
+    const void* v_new = nullptr;
+    const uint64_t* new_slots = nullptr;
+    uint64_t* table_out = nullptr;
 };
 uint64_t decode_workspace_bytes(const CacheView& c, uint64_t batch, uint32_t q_heads,
                                 uint64_t max_len, uint32_t pages_per_split);

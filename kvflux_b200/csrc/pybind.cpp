@@ -9,6 +9,7 @@
 #include <cstdint>
 
 #include "kvflux/v2/batch_block_table.h"
+#include "kvflux/v2/batch_decode_session.h"
 #include "kvflux/v2/copy_on_write.h"
 #include "kvflux/v2/paged_attention.h"
 #include "kvflux/v2/paged_kv_read.h"
@@ -231,6 +232,20 @@ PYBIND11_MODULE(_C, m) {
         .def(py::init<PhysicalBlockPool&>(), py::keep_alive<1, 2>())
         .def("attach_cached_prefix", &PrefixCache::attach_cached_prefix)
         .def("publish_computed_block", &PrefixCache::publish_computed_block);
+
+    py::class_<BatchDecodeSession>(m, "BatchDecodeSession")
+        .def(py::init<const PagedKVStorage&, std::vector<SequenceState*>, std::size_t>(), py::keep_alive<1, 2>(),
+             py::keep_alive<1, 3>())
+        .def("step", [](BatchDecodeSession& b, py::object k, py::object v, py::object q, py::object o) {
+            return b.step(ptr<const void>(k), ptr<const void>(v), ptr<const float>(q), ptr<float>(o));
+        })
+        .def("refresh", &BatchDecodeSession::refresh)
+        .def("refresh_all", &BatchDecodeSession::refresh_all)
+        .def("batch_size", &BatchDecodeSession::batch_size)
+        .def("table_width", &BatchDecodeSession::table_width)
+        .def("device_table", [](const BatchDecodeSession& b) {
+            return reinterpret_cast<std::uintptr_t>(b.device_table());
+        });
 
     py::class_<SequenceLifecycle>(m, "SequenceLifecycle")
         .def(py::init<RequestID, PhysicalBlockPool&, PagedKVStorage&, std::size_t>(), py::keep_alive<1, 3>(),
