@@ -526,6 +526,92 @@ class WriteGather:
         return (time.perf_counter() - t) * 1e3 / steps, 2 * kh.numel() * 2 + len(slots) * 8
 
 
+def layer_batches(kv, w, rank: int, world: int, ranks: Ranks, layers: int = 32) -> dict:
+    """Config 2's step across a model's layers (Llama-3-8B: 32 layers, 8 KV
+    heads x 128, bf16), one PagedKVStorage per layer on one odd/even
+    fragmented pool of 8192 pages: 64 sequences of 1024 tokens. Write: the
+    step's 256 new tokens (the last 4 of each sequence) into every layer in
+    one kvfx_write_layers launch. Gather: every sequence's K/V of every layer
+    to contiguous per-layer runs in one kvfx_gather_layers launch. The caches
+    hold whatever the allocation held: the timing does not depend on the
+    values (the tests check the bytes)."""
+    import torch
+
+    heads, hd, bs = 8 // world, 128, 16
+    nseq, total, new = 64, 1024, 4
+    b = w.decode_batch_on_pool(8192, bs, [total] * nseq, seed=0xC0F2 + rank, mode="odd")
+    dev = torch.cuda.current_device()
+    stores = [kv.PagedKVStorage(b.pool, heads, hd, kv.DType.BFloat16, dev) for _ in range(layers)]
+    arr = (kv.KvfxCache * layers)(*[kv.cache_descriptor(st) for st in stores])
+    slots = np.array(kv.build_slot_mapping([(s, p) for s in b.sequences for p in range(total - new, total)]),
+                     np.uint64)
+    n = len(slots)
+    slots_d = torch.from_numpy(slots.view(np.int64)).cuda()
+    row = heads * hd * 2
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0xC0F2 * 3 + rank)
+    k_new = torch.randn(layers * n * heads * hd, generator=gen, device="cuda").to(torch.bfloat16)
+    v_new = torch.randn_like(k_new, dtype=torch.float32).to(torch.bfloat16)
+    table, width = b.table()
+    table_d = torch.from_numpy(table.view(np.int64)).cuda()
+    lens_d = torch.full((nseq,), total, dtype=torch.int64, device="cuda")
+    per_layer = total * row
+    k_out = torch.empty(nseq * layers * per_layer, dtype=torch.uint8, device="cuda")
+    v_out = torch.empty_like(k_out)
+    kp = torch.tensor([k_out.data_ptr() + i * layers * per_layer for i in range(nseq)], dtype=torch.int64,
+                      device="cuda")
+    vp = torch.tensor([v_out.data_ptr() + i * layers * per_layer for i in range(nseq)], dtype=torch.int64,
+                      device="cuda")
+
+    def write(stream):
+        kv.check(kv.lib.kvfx_write_layers(arr, layers, k_new.data_ptr(), v_new.data_ptr(), n * row,
+                                          slots_d.data_ptr(), n, stream), "kvfx_write_layers")
+
+    def gather(stream):
+        kv.check(kv.lib.kvfx_gather_layers(arr, layers, table_d.data_ptr(), lens_d.data_ptr(), nseq, width,
+                                           kp.data_ptr(), vp.data_ptr(), per_layer, stream), "kvfx_gather_layers")
+
+    _, tot_w = time_launches(write, 50, 5, ranks)
+    _, tot_g = time_launches(gather, 10, 3, ranks)
+    # Back-to-back launches inside a CUDA graph: the device rate without the
+    # host's per-launch cost (a host launch takes about as long as this kernel).
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        write(s.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        for _ in range(50):
+            write(s.cuda_stream)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    ranks.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del graph
+    wg_ms = ranks.reduce(e0.elapsed_time(e1) / 250, "max")
+    w_ms = ranks.reduce(tot_w / 50, "max")
+    g_ms = ranks.reduce(tot_g / 10, "max")
+    peak = load_peak()[0]
+    w_bytes = ranks.reduce(float(layers * (n * row * 2 * 2 + n * 8)), "sum")
+    g_bytes = ranks.reduce(float(layers * nseq * total * row * 2 * 2 + table.nbytes), "sum")
+    out = {"workload": f"{layers} layers x config2 shapes (8 KV heads x 128 bf16), one storage per layer on one "
+                       f"8192-page odd/even pool, 64 sequences x 1024 tokens",
+           "write_tokens": n, "write_ms_per_launch": w_ms, "write_layer_tokens_per_s": layers * n / (w_ms * 1e-3),
+           "write_gbs": w_bytes / (w_ms * 1e-3) / 1e9, "write_frac_of_peak": w_bytes / (w_ms * 1e-3) / 1e9 / peak,
+           "write_graph_ms_per_launch": wg_ms, "write_graph_gbs": w_bytes / (wg_ms * 1e-3) / 1e9,
+           "write_graph_frac_of_peak": w_bytes / (wg_ms * 1e-3) / 1e9 / peak,
+           "gather_ms_per_launch": g_ms, "gather_gbs": g_bytes / (g_ms * 1e-3) / 1e9,
+           "gather_frac_of_peak": g_bytes / (g_ms * 1e-3) / 1e9 / peak}
+    del stores, k_out, v_out
+    return out
+
+
 class Prefill:
     """Config 4 on one GPU: 8 sequences x 4096 tokens, 32 Q / 8 KV heads,
     hd 128, bf16. Sequence 0 is written to 2056 tokens (128 full pages + a
@@ -711,6 +797,9 @@ def only_case(args, ranks: Ranks, kv, w, peak: float) -> int:
         wl = Decode(kv, w, cfg, ranks.rank, ranks.world)
         out = decode_step(kv, wl, args.steps, args.warmup, ranks)
         out.update({"case": args.only, "batch": cfg["batch"], "gbs": out["fused_kv_gbs"]})
+    elif args.only == "layers":
+        out = layer_batches(kv, w, ranks.rank, ranks.world, ranks, layers=args.batch or 32)
+        out.update({"case": args.only, "gbs": out["gather_gbs"]})
     elif args.only == "prefill4":
         pf = Prefill(kv, w, w.CONFIG4)
         per, total = time_launches(pf.launch, args.steps, args.warmup, ranks)
@@ -748,7 +837,7 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="headline decode only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather", "prefill4", "step5"],
+    ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather", "prefill4", "step5", "layers"],
                     help="run one kernel's case alone (profiling runs); prints a short JSON line")
     ap.add_argument("--batch", type=int, default=None, help="override the batch: decode requests, write/gather sequences (profiling runs)")
     args = ap.parse_args(argv)
@@ -850,6 +939,8 @@ def main(argv=None) -> int:
             "kv_gbs": kv3 / (ms3 * 1e-3) / 1e9, "ms_per_step": ms3,
             "frac_of_peak": alg3 / (ms3 * 1e-3) / 1e9 / peak}
         del w3
+        torch.cuda.empty_cache()
+        secondary["layers_cfg2"] = layer_batches(kv, w, rank, world, ranks)
         torch.cuda.empty_cache()
         if rank == 0:
             pf = Prefill(kv, w, w.CONFIG4)

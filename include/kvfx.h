@@ -43,6 +43,9 @@ extern "C" {
 #define KVFX_BF16 1
 #define KVFX_F32 2
 
+/* Most layers one kvfx_write_layers / kvfx_gather_layers call takes. */
+#define KVFX_MAX_LAYERS 128u
+
 /* Bits of the per-device status word. */
 #define KVFX_FLAG_BAD_INDEX 1u  /* a slot/block id beyond the cache was skipped */
 #define KVFX_FLAG_TIMEOUT 2u    /* a bounded wait inside a kernel expired        */
@@ -86,6 +89,31 @@ int kvfx_gather(const kvfx_cache* cache, const uint64_t* blocks, uint64_t num_to
 int kvfx_gather_batch(const kvfx_cache* cache, const uint64_t* blocks,
                       const uint64_t* seq_lens, uint64_t batch, uint64_t max_blocks_per_seq,
                       void* const* k_out, void* const* v_out, void* stream);
+
+/*
+ * Layer batches. A model keeps one cache per layer, all with one shape and
+ * one page pool (the reference's multi-layer plan: one PagedKVStorage per
+ * layer over one PhysicalBlockPool, docs/v2_paged_kv_storage.md:19), so a
+ * slot or a page id means the same place in every layer. These two calls
+ * move one step's rows (or a batch of sequences) for every layer in one
+ * launch, e.g. the whole KV of a request arriving from a prefill instance or
+ * leaving for host memory. caches: host array of num_layers (<=
+ * KVFX_MAX_LAYERS) descriptors equal in all fields but k_base and v_base.
+ * No counterpart in the reference, which writes and reads one layer per call.
+ */
+
+/* kvfx_write on every layer: layer l's rows are k_new/v_new + l * layer_stride_bytes
+ * ([num_tokens][num_kv_heads][head_size] each; layer_stride_bytes >= that size). */
+int kvfx_write_layers(const kvfx_cache* caches, uint32_t num_layers, const void* k_new,
+                      const void* v_new, uint64_t layer_stride_bytes, const uint64_t* slots,
+                      uint64_t num_tokens, void* stream);
+
+/* kvfx_gather_batch on every layer: sequence b's layer l goes to
+ * k_out[b] + l * out_layer_stride_bytes (and v_out alike). */
+int kvfx_gather_layers(const kvfx_cache* caches, uint32_t num_layers, const uint64_t* blocks,
+                       const uint64_t* seq_lens, uint64_t batch, uint64_t max_blocks_per_seq,
+                       void* const* k_out, void* const* v_out, uint64_t out_layer_stride_bytes,
+                       void* stream);
 
 /*
  * Whole-page copy of K and V from src_block to dst_block (byte-exact).

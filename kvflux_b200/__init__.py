@@ -8,7 +8,8 @@ Two native surfaces, both built in-tree by ``python kvflux_b200/build.py``:
   (PhysicalBlockPool, SequenceState, PagedKVStorage, write_paged_kv,
   read_paged_kv, paged_attention, paged_attention_batch, append_token_cow,
   PrefixCache, SequenceLifecycle, ...) running on those kernels, plus
-  BatchDecodeSession (batched decode steps over a device-resident block table).
+  BatchDecodeSession (batched decode steps over a device-resident block table)
+  and write_paged_kv_layers / read_paged_kv_layers (one launch for all layers).
 
 There is no fallback: importing fails loudly if the extension is not built.
 """
@@ -34,6 +35,7 @@ vp = ctypes.c_void_p
 KVFX_OK, KVFX_EINVAL, KVFX_ERANGE, KVFX_EOVERFLOW, KVFX_ECUDA, KVFX_ETIMEOUT, KVFX_ENOSPACE = range(7)
 KVFX_F16, KVFX_BF16, KVFX_F32 = 0, 1, 2
 KVFX_FLAG_BAD_INDEX, KVFX_FLAG_TIMEOUT = 1, 2
+KVFX_MAX_LAYERS = 128
 
 
 class KvfxCache(ctypes.Structure):
@@ -59,6 +61,8 @@ def _load():
     L.kvfx_gather.argtypes = [C, vp, u64, vp, vp, vp]
     L.kvfx_gather_batch.argtypes = [C, vp, vp, u64, u64, vp, vp, vp]
     L.kvfx_copy_page.argtypes = [C, u64, u64, vp]
+    L.kvfx_write_layers.argtypes = [C, u32, vp, vp, u64, vp, u64, vp]
+    L.kvfx_gather_layers.argtypes = [C, u32, vp, vp, u64, u64, vp, vp, u64, vp]
     L.kvfx_decode_workspace_bytes.argtypes = [C, u64, u32, u64, u32]
     L.kvfx_decode_workspace_bytes.restype = u64
     L.kvfx_decode_pages_per_split.argtypes = [C, u64, u32, u64, u64]
@@ -81,7 +85,7 @@ lib = _load()
 
 #: Every symbol include/kvfx.h declares (checked by the tests).
 KVFX_SYMBOLS = (
-    "kvfx_write", "kvfx_gather", "kvfx_gather_batch", "kvfx_copy_page", "kvfx_decode_workspace_bytes",
+    "kvfx_write", "kvfx_gather", "kvfx_gather_batch", "kvfx_write_layers", "kvfx_gather_layers", "kvfx_copy_page", "kvfx_decode_workspace_bytes",
     "kvfx_decode_pages_per_split", "kvfx_decode", "kvfx_decode_append", "kvfx_decode_noalloc", "kvfx_attention_workspace_bytes",
     "kvfx_attention",
     "kvfx_last_error", "kvfx_device_status", "kvfx_version",

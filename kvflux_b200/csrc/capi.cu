@@ -199,6 +199,87 @@ int kvfx_gather_batch(const kvfx_cache* cache, const uint64_t* blocks, const uin
     return e == cudaSuccess ? KVFX_OK : cuda_fail("paged KV batched gather launch", e);
 }
 
+// Views of num_layers caches that must agree in everything but their bases.
+int make_layer_views(const kvfx_cache* caches, uint32_t num_layers, kvfx::CacheView* views) {
+    if (caches == nullptr) return fail(KVFX_EINVAL, "caches array is null");
+    if (num_layers > KVFX_MAX_LAYERS) return fail(KVFX_EINVAL, "more than KVFX_MAX_LAYERS layers");
+    for (uint32_t l = 0; l < num_layers; ++l) {
+        if (int rc = make_view(caches + l, views + l); rc != KVFX_OK) return rc;
+        const kvfx::CacheView& a = views[0];
+        const kvfx::CacheView& b = views[l];
+        if (b.num_blocks != a.num_blocks || b.heads != a.heads || b.bs != a.bs || b.hd != a.hd ||
+            b.dtype != a.dtype || b.device != a.device) {
+            return fail(KVFX_EINVAL, "layer caches differ in shape, dtype or device");
+        }
+    }
+    return KVFX_OK;
+}
+
+int kvfx_write_layers(const kvfx_cache* caches, uint32_t num_layers, const void* k_new, const void* v_new,
+                      uint64_t layer_stride_bytes, const uint64_t* slots, uint64_t num_tokens, void* stream) {
+    kvfx::CacheView views[KVFX_MAX_LAYERS];
+    if (int rc = make_layer_views(caches, num_layers, views); rc != KVFX_OK) return rc;
+    if (num_layers == 0 || num_tokens == 0) return KVFX_OK;
+    if (k_new == nullptr || v_new == nullptr || slots == nullptr) {
+        return fail(KVFX_EINVAL, "k_new, v_new and slots must be non-null");
+    }
+    const kvfx::CacheView& c = views[0];
+    uint64_t rows = 0, bytes = 0, span = 0;
+    if (!mul_ok(num_tokens, c.heads, &rows) || !mul_ok(rows, c.row_bytes, &bytes) ||
+        !mul_ok(layer_stride_bytes, num_layers - 1, &span) || span + bytes < span) {
+        return fail(KVFX_EOVERFLOW, "layered write size overflows");
+    }
+    if (num_layers > 1 && layer_stride_bytes < bytes) {
+        return fail(KVFX_EINVAL, "layer_stride_bytes is smaller than one layer's rows");
+    }
+    DeviceScope scope(c.device);
+    if (scope.error() != cudaSuccess) return cuda_fail("select device", scope.error());
+    const cudaError_t e = kvfx::launch_write_layers(views, num_layers, k_new, v_new, layer_stride_bytes, slots,
+                                                    num_tokens, status_word(c.device),
+                                                    static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? KVFX_OK : cuda_fail("layered paged KV write launch", e);
+}
+
+int kvfx_gather_layers(const kvfx_cache* caches, uint32_t num_layers, const uint64_t* blocks,
+                       const uint64_t* seq_lens, uint64_t batch, uint64_t max_blocks_per_seq,
+                       void* const* k_out, void* const* v_out, uint64_t out_layer_stride_bytes, void* stream) {
+    kvfx::CacheView views[KVFX_MAX_LAYERS];
+    if (int rc = make_layer_views(caches, num_layers, views); rc != KVFX_OK) return rc;
+    if (num_layers == 0 || batch == 0 || max_blocks_per_seq == 0) return KVFX_OK;
+    if (blocks == nullptr || seq_lens == nullptr || k_out == nullptr || v_out == nullptr) {
+        return fail(KVFX_EINVAL, "blocks, seq_lens, k_out and v_out must be non-null");
+    }
+    if (batch > 65535) return fail(KVFX_EINVAL, "batch above 65535 sequences per launch");
+    const kvfx::CacheView& c = views[0];
+    uint64_t max_len = 0, per_seq = 0, tmp = 0, span = 0;
+    if (!mul_ok(max_blocks_per_seq, c.bs, &max_len) || !mul_ok(max_len, c.heads, &tmp) ||
+        !mul_ok(tmp, c.row_bytes, &per_seq) || !mul_ok(out_layer_stride_bytes, num_layers - 1, &span)) {
+        return fail(KVFX_EOVERFLOW, "layered gather size overflows");
+    }
+    DeviceScope scope(c.device);
+    if (scope.error() != cudaSuccess) return cuda_fail("select device", scope.error());
+    kvfx::GatherArgs a{};
+    a.blocks = blocks;
+    a.lens = seq_lens;
+    a.batch = batch;
+    a.max_blocks = max_blocks_per_seq;
+    a.k_out_list = k_out;
+    a.v_out_list = v_out;
+    a.max_len = max_len;
+    unsigned* st = status_word(c.device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = kvfx::launch_gather_layers(views, num_layers, a, out_layer_stride_bytes, st, s);
+    if (e == cudaErrorNotSupported) {  // rows or alignments the 16-byte kernel cannot take: per layer
+        e = cudaSuccess;
+        a.force_simt = true;
+        for (uint32_t l = 0; l < num_layers && e == cudaSuccess; ++l) {
+            a.out_offset = l * out_layer_stride_bytes;
+            e = kvfx::launch_gather(views[l], a, st, s);
+        }
+    }
+    return e == cudaSuccess ? KVFX_OK : cuda_fail("layered paged KV gather launch", e);
+}
+
 int kvfx_copy_page(const kvfx_cache* cache, uint64_t src_block, uint64_t dst_block, void* stream) {
     kvfx::CacheView c;
     if (int rc = make_view(cache, &c); rc != KVFX_OK) return rc;

@@ -109,14 +109,14 @@ template <int VB>
 __global__ void __launch_bounds__(256) gather_simt_kernel(
     const typename Vec<VB>::T* __restrict__ k_cache, const typename Vec<VB>::T* __restrict__ v_cache,
     const uint64_t* __restrict__ blocks, uint64_t max_blocks, const uint64_t* __restrict__ lens,
-    uint64_t single_len, void* const* k_list, void* const* v_list, void* k_one, void* v_one,
+    uint64_t single_len, void* const* k_list, void* const* v_list, void* k_one, void* v_one, uint64_t out_offset,
     uint32_t heads, uint32_t bs, uint32_t vpr, uint64_t num_blocks, unsigned* status) {
     using V = typename Vec<VB>::T;
     const uint64_t b = blockIdx.y;
     const uint64_t len = lens != nullptr ? lens[b] : single_len;
     const uint64_t* row_blocks = blocks + b * max_blocks;
-    V* k_out = static_cast<V*>(k_list != nullptr ? k_list[b] : k_one);
-    V* v_out = static_cast<V*>(v_list != nullptr ? v_list[b] : v_one);
+    V* k_out = reinterpret_cast<V*>(static_cast<char*>(k_list != nullptr ? k_list[b] : k_one) + out_offset);
+    V* v_out = reinterpret_cast<V*>(static_cast<char*>(v_list != nullptr ? v_list[b] : v_one) + out_offset);
     if (((reinterpret_cast<uintptr_t>(k_out) | reinterpret_cast<uintptr_t>(v_out)) % VB) != 0) {
         // Batched outputs are only known on the device: refuse a misaligned one.
         if (threadIdx.x == 0 && blockIdx.x == 0) raise_flag(status, KVFX_FLAG_BAD_INDEX);
@@ -158,7 +158,7 @@ cudaError_t gather_simt_vb(const CacheView& c, const GatherArgs& a, unsigned* st
     dim3 grid(std::max<uint32_t>(gx, 1), static_cast<uint32_t>(a.batch));
     gather_simt_kernel<VB><<<grid, 256, 0, s>>>(
         reinterpret_cast<const V*>(c.k), reinterpret_cast<const V*>(c.v), a.blocks, a.max_blocks,
-        a.lens, a.single_len, a.k_out_list, a.v_out_list, a.k_out, a.v_out, c.heads, c.bs,
+        a.lens, a.single_len, a.k_out_list, a.v_out_list, a.k_out, a.v_out, a.out_offset, c.heads, c.bs,
         static_cast<uint32_t>(vpr), c.num_blocks, status);
     return cudaGetLastError();
 }
@@ -190,6 +190,39 @@ FastDiv make_fastdiv(uint32_t d) {
 }
 
 __device__ __forceinline__ uint32_t fast_div(uint32_t n, FastDiv f) { return (__umulhi(n, f.m) + n) >> f.s; }
+
+// One page of one sequence: n output vectors (tokens of the page x heads x
+// row vectors) from the page's K/V blocks ks/vs to the runs kd/vd; the same
+// loop as gather_direct_kernel's (kept written out there: as a call it costs
+// that kernel 16 registers and a CTA per SM).
+__device__ __forceinline__ void gather_page(const uint4* ks, const uint4* vs,
+                                            uint4* kd, uint4* vd, uint32_t n,
+                                            uint32_t bs, uint32_t vpr, uint32_t vpt, FastDiv div_vpt,
+                                            FastDiv div_vpr, uint32_t tid) {
+    for (uint32_t base = 0; base < n; base += kGatherDirectThreads * kGatherDirectPer) {
+        uint4 kx[kGatherDirectPer], vx[kGatherDirectPer];
+#pragma unroll
+        for (int i = 0; i < kGatherDirectPer; ++i) {
+            const uint32_t e = base + i * kGatherDirectThreads + tid;
+            if (e < n) {
+                const uint32_t t = fast_div(e, div_vpt);
+                const uint32_t r = e - t * vpt;
+                const uint32_t h = fast_div(r, div_vpr);
+                const uint32_t src = (h * bs + t) * vpr + (r - h * vpr);
+                kx[i] = __ldg(ks + src);
+                vx[i] = __ldg(vs + src);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kGatherDirectPer; ++i) {
+            const uint32_t e = base + i * kGatherDirectThreads + tid;
+            if (e < n) {
+                __stcs(kd + e, kx[i]);
+                __stcs(vd + e, vx[i]);
+            }
+        }
+    }
+}
 
 __global__ void __launch_bounds__(kGatherDirectThreads) gather_direct_kernel(
     const uint4* __restrict__ k_cache, const uint4* __restrict__ v_cache,
@@ -253,6 +286,104 @@ __global__ void __launch_bounds__(kGatherDirectThreads) gather_direct_kernel(
     }
 }
 
+// ---------------------------------------------------------- layer batches ---
+// One launch over the caches of num_layers layers that share a page pool
+// (one PagedKVStorage per layer): blockIdx.y (write) or blockIdx.z (gather)
+// selects the layer, whose cache bases come from the kernel parameters.
+struct LayerBases {
+    char* k[KVFX_MAX_LAYERS];
+    char* v[KVFX_MAX_LAYERS];
+};
+
+constexpr int kWriteLayersPer = 4;
+
+__global__ void __launch_bounds__(256) write_layers_kernel(
+    const __grid_constant__ LayerBases bases, const uint4* __restrict__ k_new, const uint4* __restrict__ v_new,
+    uint64_t layer_stride_vecs, const uint64_t* __restrict__ slots, uint32_t total, uint32_t heads, uint32_t vpr,
+    uint32_t bs, uint64_t slot_count, unsigned* status) {
+    const uint32_t layer = blockIdx.y;
+    const uint4* kn = k_new + layer * layer_stride_vecs;
+    const uint4* vn = v_new + layer * layer_stride_vecs;
+    uint4* kc = reinterpret_cast<uint4*>(bases.k[layer]);
+    uint4* vc = reinterpret_cast<uint4*>(bases.v[layer]);
+    // Each thread has kWriteLayersPer vectors of K and of V in flight before
+    // it stores any (vector i = base + j * 256 + tid, in input order).
+    const uint32_t span = gridDim.x * blockDim.x * kWriteLayersPer;
+    for (uint32_t base = blockIdx.x * blockDim.x * kWriteLayersPer; base < total; base += span) {
+        uint4 kx[kWriteLayersPer], vx[kWriteLayersPer];
+        uint64_t dst[kWriteLayersPer];
+#pragma unroll
+        for (int j = 0; j < kWriteLayersPer; ++j) {
+            const uint32_t i = base + j * blockDim.x + threadIdx.x;
+            dst[j] = ~0ull;
+            if (i < total) {
+                const uint32_t row = i / vpr;
+                const uint32_t c = i - row * vpr;
+                const uint32_t tok = row / heads;
+                const uint32_t h = row - tok * heads;
+                const uint64_t slot = __ldg(slots + tok);
+                if (slot < slot_count) {
+                    const uint64_t page = slot / bs;
+                    const uint64_t off = slot - page * bs;
+                    dst[j] = ((page * heads + h) * bs + off) * vpr + c;
+                    kx[j] = __ldg(kn + i);
+                    vx[j] = __ldg(vn + i);
+                } else {
+                    raise_flag(status, KVFX_FLAG_BAD_INDEX);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kWriteLayersPer; ++j) {
+            if (dst[j] != ~0ull) {
+                kc[dst[j]] = kx[j];
+                vc[dst[j]] = vx[j];
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kGatherDirectThreads) gather_layers_kernel(
+    const __grid_constant__ LayerBases bases, const uint64_t* __restrict__ blocks, uint64_t max_blocks,
+    const uint64_t* __restrict__ lens, void* const* k_list, void* const* v_list, uint64_t out_layer_stride,
+    uint32_t heads, uint32_t bs, uint32_t vpr, FastDiv div_vpt, FastDiv div_vpr, uint64_t num_blocks,
+    unsigned* status) {
+    const uint32_t tid = threadIdx.x;
+    const uint64_t b = blockIdx.y;
+    const uint32_t layer = blockIdx.z;
+    const uint64_t len = lens[b];
+    if (len == 0) return;
+    const uint64_t* row_blocks = blocks + b * max_blocks;
+    char* kb = static_cast<char*>(k_list[b]);
+    char* vb = static_cast<char*>(v_list[b]);
+    if (((reinterpret_cast<uintptr_t>(kb) | reinterpret_cast<uintptr_t>(vb)) & 15u) != 0) {
+        if (tid == 0 && blockIdx.x == 0) raise_flag(status, KVFX_FLAG_BAD_INDEX);
+        return;
+    }
+    uint4* k_out = reinterpret_cast<uint4*>(kb + layer * out_layer_stride);
+    uint4* v_out = reinterpret_cast<uint4*>(vb + layer * out_layer_stride);
+    const uint64_t pages = ceil_div(len, bs);
+    if (pages > max_blocks) {
+        if (tid == 0 && blockIdx.x == 0) raise_flag(status, KVFX_FLAG_BAD_INDEX);
+        return;
+    }
+    const uint32_t vpt = heads * vpr;
+    const uint64_t page_vecs = static_cast<uint64_t>(bs) * vpt;
+    const uint4* k_cache = reinterpret_cast<const uint4*>(bases.k[layer]);
+    const uint4* v_cache = reinterpret_cast<const uint4*>(bases.v[layer]);
+    for (uint64_t j = blockIdx.x; j < pages; j += gridDim.x) {
+        const uint64_t blk = __ldg(row_blocks + j);
+        if (blk >= num_blocks) {
+            if (tid == 0) raise_flag(status, KVFX_FLAG_BAD_INDEX);
+            continue;
+        }
+        const uint64_t t0 = j * bs;
+        const uint32_t n = static_cast<uint32_t>(umin64(bs, len - t0)) * vpt;
+        gather_page(k_cache + blk * page_vecs, v_cache + blk * page_vecs, k_out + t0 * vpt, v_out + t0 * vpt, n,
+                    bs, vpr, vpt, div_vpt, div_vpr, tid);
+    }
+}
+
 }  // namespace
 
 uint32_t vector_width(uint64_t bytes, const void* const* ptrs, int n) {
@@ -279,6 +410,62 @@ cudaError_t launch_write(const CacheView& c, const void* k_new, const void* v_ne
     }
 }
 
+cudaError_t launch_write_layers(const CacheView* layers, uint32_t num_layers, const void* k_new,
+                                const void* v_new, uint64_t layer_stride, const uint64_t* slots, uint64_t n,
+                                unsigned* status, cudaStream_t s) {
+    const CacheView& c = layers[0];
+    const uint64_t total = n * c.heads * (c.row_bytes / 16);
+    bool vec16 = c.row_bytes % 16 == 0 && layer_stride % 16 == 0 && total < (1ull << 31) &&
+                 ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15u) == 0;
+    for (uint32_t l = 0; l < num_layers && vec16; ++l) {
+        vec16 = ((reinterpret_cast<uintptr_t>(layers[l].k) | reinterpret_cast<uintptr_t>(layers[l].v)) & 15u) == 0;
+    }
+    if (!vec16) {  // odd rows or alignments: one launch per layer
+        for (uint32_t l = 0; l < num_layers; ++l) {
+            const cudaError_t e = launch_write(layers[l], static_cast<const char*>(k_new) + l * layer_stride,
+                                               static_cast<const char*>(v_new) + l * layer_stride, slots, n,
+                                               status, s);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
+    }
+    LayerBases bases{};
+    for (uint32_t l = 0; l < num_layers; ++l) {
+        bases.k[l] = layers[l].k;
+        bases.v[l] = layers[l].v;
+    }
+    const uint32_t gx = static_cast<uint32_t>(std::max<uint64_t>(
+        1, std::min<uint64_t>(ceil_div(total, 256 * kWriteLayersPer), ceil_div(148ull * 16, num_layers))));
+    write_layers_kernel<<<dim3(gx, num_layers), 256, 0, s>>>(
+        bases, static_cast<const uint4*>(k_new), static_cast<const uint4*>(v_new), layer_stride / 16, slots,
+        static_cast<uint32_t>(total), c.heads, static_cast<uint32_t>(c.row_bytes / 16), c.bs, c.slot_count, status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather_layers(const CacheView* layers, uint32_t num_layers, const GatherArgs& a,
+                                 uint64_t out_layer_stride, unsigned* status, cudaStream_t s) {
+    if (a.batch == 0 || a.max_len == 0) return cudaSuccess;
+    const CacheView& c = layers[0];
+    bool direct = c.row_bytes % 16 == 0 && c.page_bytes / 16 < (1ull << 31) && out_layer_stride % 16 == 0;
+    for (uint32_t l = 0; l < num_layers && direct; ++l) {
+        direct = ((reinterpret_cast<uintptr_t>(layers[l].k) | reinterpret_cast<uintptr_t>(layers[l].v)) & 15u) == 0;
+    }
+    if (!direct) return cudaErrorNotSupported;  // the C ABI routes these shapes per layer
+    LayerBases bases{};
+    for (uint32_t l = 0; l < num_layers; ++l) {
+        bases.k[l] = layers[l].k;
+        bases.v[l] = layers[l].v;
+    }
+    const uint32_t vpr = static_cast<uint32_t>(c.row_bytes / 16);
+    const uint64_t pages_max = ceil_div(a.max_len, c.bs);
+    dim3 grid(static_cast<uint32_t>(std::min<uint64_t>(pages_max, 0x7fffffffu)), static_cast<uint32_t>(a.batch),
+              num_layers);
+    gather_layers_kernel<<<grid, kGatherDirectThreads, 0, s>>>(
+        bases, a.blocks, a.max_blocks, a.lens, a.k_out_list, a.v_out_list, out_layer_stride, c.heads, c.bs, vpr,
+        make_fastdiv(c.heads * vpr), make_fastdiv(vpr), c.num_blocks, status);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_copy_page(const CacheView& c, uint64_t src, uint64_t dst, unsigned*,
                              cudaStream_t s) {
     const void* ptrs[2] = {c.k, c.v};
@@ -298,7 +485,7 @@ cudaError_t launch_gather(const CacheView& c, const GatherArgs& a, unsigned* sta
     // 31 bits. Batched outputs are only known on the device: the kernel
     // refuses a misaligned one with the bad-index flag.
     const bool single = a.k_out_list == nullptr;
-    bool direct = c.row_bytes % 16 == 0 && c.page_bytes / 16 < (1ull << 31) &&
+    bool direct = !a.force_simt && a.out_offset == 0 && c.row_bytes % 16 == 0 && c.page_bytes / 16 < (1ull << 31) &&
                   (reinterpret_cast<uintptr_t>(c.k) | reinterpret_cast<uintptr_t>(c.v)) % 16 == 0;
     if (direct && single) {
         direct = reinterpret_cast<uintptr_t>(a.k_out) % 16 == 0 && reinterpret_cast<uintptr_t>(a.v_out) % 16 == 0;
@@ -315,7 +502,9 @@ cudaError_t launch_gather(const CacheView& c, const GatherArgs& a, unsigned* sta
         return cudaGetLastError();
     }
     const void* ptrs[4] = {c.k, c.v, single ? a.k_out : nullptr, single ? a.v_out : nullptr};
-    switch (vector_width(c.row_bytes, ptrs, single ? 4 : 2)) {
+    uint32_t width = vector_width(c.row_bytes, ptrs, single ? 4 : 2);
+    while (width > 1 && a.out_offset % width != 0) width /= 2;
+    switch (width) {
     case 16: return gather_simt_vb<16>(c, a, status, s);
     case 8: return gather_simt_vb<8>(c, a, status, s);
     case 4: return gather_simt_vb<4>(c, a, status, s);

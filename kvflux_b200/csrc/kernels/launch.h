@@ -36,6 +36,12 @@ cudaError_t launch_write(const CacheView& c, const void* k_new, const void* v_ne
 cudaError_t launch_copy_page(const CacheView& c, uint64_t src, uint64_t dst, unsigned* status,
                              cudaStream_t s);
 
+// Layer batches over caches of one shape (layers[0..num_layers), at most
+// KVFX_MAX_LAYERS): layer l's new rows start at k_new + l * layer_stride bytes.
+cudaError_t launch_write_layers(const CacheView* layers, uint32_t num_layers, const void* k_new,
+                                const void* v_new, uint64_t layer_stride, const uint64_t* slots, uint64_t n,
+                                unsigned* status, cudaStream_t s);
+
 // Gather of `batch` sequences. If `per_seq_out` is false, k_out/v_out point to
 // a single sequence's outputs (batch must be 1) and `single_blocks`/`single_len`
 // describe it; otherwise k_out/v_out are device arrays of device pointers and
@@ -50,8 +56,15 @@ struct GatherArgs {
     void* k_out;               // single-sequence outputs
     void* v_out;
     uint64_t max_len;          // host bound of the lengths (grid sizing)
+    uint64_t out_offset = 0;   // bytes added to every output pointer (SIMT kernel only)
+    bool force_simt = false;   // take the element-wise kernel (needed for out_offset != 0)
 };
 cudaError_t launch_gather(const CacheView& c, const GatherArgs& a, unsigned* status, cudaStream_t s);
+// Batched gather of every layer (a.k_out_list / a.v_out_list per sequence;
+// layer l at + l * out_layer_stride bytes). Returns cudaErrorNotSupported for
+// rows or alignments the 16-byte kernel cannot take (no launch).
+cudaError_t launch_gather_layers(const CacheView* layers, uint32_t num_layers, const GatherArgs& a,
+                                 uint64_t out_layer_stride, unsigned* status, cudaStream_t s);
 
 struct DecodeArgs {
     const float* q;

@@ -12,6 +12,7 @@
 #include "kvflux/v2/batch_decode_session.h"
 #include "kvflux/v2/copy_on_write.h"
 #include "kvflux/v2/paged_attention.h"
+#include "kvflux/v2/paged_kv_layers.h"
 #include "kvflux/v2/paged_kv_read.h"
 #include "kvflux/v2/paged_kv_storage.h"
 #include "kvflux/v2/paged_kv_write.h"
@@ -227,6 +228,14 @@ PYBIND11_MODULE(_C, m) {
         paged_attention_batch(s, seqs, ptr<const float>(q), ptr<float>(o), query_heads);
     });
     m.def("append_token_cow", &append_token_cow);
+    m.def("write_paged_kv_layers", [](const std::vector<PagedKVStorage*>& layers, py::object k, py::object v,
+                                      const SlotMapping& slots) {
+        write_paged_kv_layers(layers, ptr<const void>(k), ptr<const void>(v), slots);
+    });
+    m.def("read_paged_kv_layers", [](const std::vector<const PagedKVStorage*>& layers, const SequenceState& seq,
+                                     py::object k, py::object v) {
+        read_paged_kv_layers(layers, seq, ptr<void>(k), ptr<void>(v));
+    });
 
     py::class_<PrefixCache>(m, "PrefixCache")
         .def(py::init<PhysicalBlockPool&>(), py::keep_alive<1, 2>())
