@@ -244,8 +244,8 @@ class Decode:
         self.o = torch.empty_like(self.q)
         self.desc = kv.cache_descriptor(self.storage)
         self.max_len = int(self.lens.max())
-        self.pps = kv.lib.kvfx_decode_pages_per_split(ctypes.byref(self.desc), self.batch, self.qh, self.max_len,
-                                                      int(self.lens.sum()))
+        self.pps = cfg.get("pages_per_split") or kv.lib.kvfx_decode_pages_per_split(
+            ctypes.byref(self.desc), self.batch, self.qh, self.max_len, int(self.lens.sum()))
         ws = kv.lib.kvfx_decode_workspace_bytes(ctypes.byref(self.desc), self.batch, self.qh, self.max_len, self.pps)
         self.ws = torch.zeros(max(int(ws), 16), dtype=torch.uint8, device="cuda")
         self.kv_bytes = int(self.lens.sum()) * self.kvh * self.hd * 2 * 2
@@ -784,12 +784,17 @@ def only_case(args, ranks: Ranks, kv, w, peak: float) -> int:
         cfg = dict(w.CONFIG5 if args.only == "decode5" else w.CONFIG3)
         if args.batch:
             cfg["batch"] = args.batch
-        wl = Decode(kv, w, cfg, ranks.rank, ranks.world)
+        if args.pps:
+            cfg["pages_per_split"] = args.pps
+        # --shard N: rank 0's KV-head shard of an N-way split, on this one GPU
+        # (every rank's shard has the same shape; only the seeds differ).
+        shard_world = args.shard or ranks.world
+        wl = Decode(kv, w, cfg, ranks.rank, shard_world)
         per, total = time_launches(wl.launch, args.steps, args.warmup, ranks)
         ms = total / args.steps
-        out = {"case": args.only, "batch": cfg["batch"], "ms_per_launch": ms, "kv_bytes": wl.kv_bytes,
-               "algorithmic_bytes": wl.alg_bytes, "gbs": wl.alg_bytes / (ms * 1e-3) / 1e9,
-               "pages_per_split": wl.pps}
+        out = {"case": args.only, "batch": cfg["batch"], "shard_of": shard_world, "ms_per_launch": ms,
+               "kv_bytes": wl.kv_bytes, "algorithmic_bytes": wl.alg_bytes,
+               "gbs": wl.alg_bytes / (ms * 1e-3) / 1e9, "pages_per_split": wl.pps}
     elif args.only == "step5":
         cfg = dict(w.CONFIG5)
         if args.batch:
@@ -840,6 +845,10 @@ def main(argv=None) -> int:
     ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather", "prefill4", "step5", "layers"],
                     help="run one kernel's case alone (profiling runs); prints a short JSON line")
     ap.add_argument("--batch", type=int, default=None, help="override the batch: decode requests, write/gather sequences (profiling runs)")
+    ap.add_argument("--shard", type=int, default=None,
+                    help="with --only decode5/decode3 on one GPU: time rank 0's shard of an N-way KV-head split")
+    ap.add_argument("--pps", type=int, default=None,
+                    help="with --only decode5/decode3: pages per split instead of the library's choice")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
