@@ -28,4 +28,16 @@ void paged_attention_batch(const PagedKVStorage& storage,
                            const float* query_device, float* output_device,
                            std::size_t query_heads);
 
+// paged_attention_batch with Q and O in page-locked host memory
+// (cudaHostAlloc / cudaHostRegister) instead of device memory; no
+// counterpart in the reference, whose batch API takes device buffers. Same
+// checks, results (bit-identical) and synchronous contract. Q goes up in row
+// chunks, each just ahead of its kernel, and the kernels write O straight
+// into the host buffer through its device mapping, so the transfers overlap
+// the attention instead of preceding and following it.
+void paged_attention_batch_host(const PagedKVStorage& storage,
+                                const std::vector<const SequenceState*>& sequences,
+                                const float* query_host, float* output_host,
+                                std::size_t query_heads);
+
 } // namespace kvflux::v2

@@ -59,8 +59,24 @@ void paged_attention(const PagedKVStorage& storage, const SequenceState& sequenc
     rt.finish("paged attention synchronize");
 }
 
-void paged_attention_batch(const PagedKVStorage& storage, const std::vector<const SequenceState*>& sequences,
-                           const float* query_device, float* output_device, std::size_t query_heads) {
+namespace {
+
+// Device address of page-locked host memory (cudaHostAlloc / cudaHostRegister),
+// or invalid_argument for anything else.
+void* pinned_device_address(const void* p, const char* name) {
+    cudaPointerAttributes a{};
+    const cudaError_t e = cudaPointerGetAttributes(&a, p);
+    if (e != cudaSuccess || a.type != cudaMemoryTypeHost || a.devicePointer == nullptr) {
+        if (e != cudaSuccess) (void)cudaGetLastError();
+        throw std::invalid_argument(std::string(name) + " must be page-locked host memory");
+    }
+    return a.devicePointer;
+}
+
+// Shared body of paged_attention_batch (device Q/O) and
+// paged_attention_batch_host (page-locked host Q/O).
+void batch_decode(const PagedKVStorage& storage, const std::vector<const SequenceState*>& sequences,
+                  const float* query_device, float* output_device, std::size_t query_heads, bool host_io) {
     const PagedKVLayout& layout = storage.layout();
     if (query_heads == 0 || query_heads % layout.num_kv_heads() != 0) {
         throw std::invalid_argument("invalid batch attention head count");
@@ -140,6 +156,15 @@ void paged_attention_batch(const PagedKVStorage& storage, const std::vector<cons
         if (query_device == nullptr || output_device == nullptr) {
             throw std::invalid_argument("Q and attention output device pointers are required");
         }
+        if (host_io) {
+            (void)pinned_device_address(query_device, "Q");
+            (void)pinned_device_address(output_device, "attention output");
+            if (detail::overlaps(query_device, tensor_bytes, output_device, tensor_bytes)) {
+                throw std::invalid_argument("Q and attention output must not overlap");
+            }
+            if (batch > 65535) throw std::invalid_argument("batch above 65535 sequences");
+            return;
+        }
         detail::require_device_pointer(query_device, storage.device(), "Q");
         detail::require_device_pointer(output_device, storage.device(), "attention output");
         if (detail::overlaps(query_device, tensor_bytes, output_device, tensor_bytes) ||
@@ -178,9 +203,24 @@ void paged_attention_batch(const PagedKVStorage& storage, const std::vector<cons
         const std::size_t b = kvfx_decode_workspace_bytes(&rt.cache, r1 - r0, qh, chunk_max(r0, r1), pps);
         return (b + 255) & ~std::size_t(255);
     };
+    // Host I/O: Q goes up per chunk into device scratch just ahead of that
+    // chunk's kernel; the kernels write O straight into the page-locked
+    // output (its device mapping), so neither copy waits for the other work.
+    const float* q_dev = query_device;
+    float* o_dev = output_device;
+    if (host_io) {
+        q_dev = static_cast<const float*>(rt.ensure_io(batch * row_elems * sizeof(float)));
+        o_dev = static_cast<float*>(pinned_device_address(output_device, "attention output"));
+    }
+    auto upload_q = [&](std::size_t r0, std::size_t r1, cudaStream_t stream) {
+        if (!host_io || r1 <= r0) return;
+        detail::cuda_check(cudaMemcpyAsync(const_cast<float*>(q_dev) + r0 * row_elems, query_device + r0 * row_elems,
+                                           (r1 - r0) * row_elems * sizeof(float), cudaMemcpyHostToDevice, stream),
+                           "upload Q");
+    };
     auto launch_rows = [&](std::size_t r0, std::size_t r1, void* ws, std::size_t ws_bytes, cudaStream_t stream) {
         detail::check_kvfx(
-            kvfx_decode(&rt.cache, query_device + r0 * row_elems, output_device + r0 * row_elems,
+            kvfx_decode(&rt.cache, q_dev + r0 * row_elems, o_dev + r0 * row_elems,
                         reinterpret_cast<const uint64_t*>(static_cast<unsigned char*>(dev[1]) + r0 * row_bytes),
                         static_cast<const uint64_t*>(dev[0]) + r0, r1 - r0, widest, qh, chunk_max(r0, r1), pps,
                         ws, ws_bytes, stream),
@@ -196,12 +236,15 @@ void paged_attention_batch(const PagedKVStorage& storage, const std::vector<cons
     // enough to cover the rest of the table (~0.2 ms of host writing, then
     // ~0.3 ms of upload while the kernel saturates HBM), and the two kernels
     // take as long as one launch over every row.
+    // With host I/O the first chunk also waits for its Q upload (measured at
+    // config 5 per call: a quarter of the rows first 2.82-2.92 ms, a third
+    // 2.85, a half 3.08, an eighth 2.96; with the second chunk's Q issued
+    // before the first chunk's table, 2.85).
     const std::size_t head_rows = batch >= 16 ? (batch + 3) / 4 : batch;
     const std::size_t ws0 = workspace_of(0, head_rows);
     const std::size_t ws1 = head_rows < batch ? workspace_of(head_rows, batch) : 0;
     auto* ws = static_cast<unsigned char*>(rt.ensure_workspace(ws0 + ws1));
-    fill_rows(0, head_rows);
-    rt.push_range(0, table_offset + head_rows * row_bytes, nullptr);
+    upload_q(0, head_rows, nullptr);
     if (head_rows < batch) {
         // The side stream does not wait for the default stream by itself:
         // order it after the caller's work (Q) issued before this call.
@@ -209,7 +252,12 @@ void paged_attention_batch(const PagedKVStorage& storage, const std::vector<cons
         detail::cuda_check(cudaEventRecord(rt.side_ready, nullptr), "record side start");
         detail::cuda_check(cudaStreamWaitEvent(rt.side, rt.side_ready, 0), "order side start");
     }
+    fill_rows(0, head_rows);
+    rt.push_range(0, table_offset + head_rows * row_bytes, nullptr);
     launch_rows(0, head_rows, ws0 ? ws : nullptr, ws0, nullptr);
+    // Issued after the first chunk's table, which would otherwise queue
+    // behind it on the copy engine.
+    if (head_rows < batch) upload_q(head_rows, batch, rt.side);
     if (head_rows < batch) {
         try {
             fill_rows(head_rows, batch);
@@ -225,6 +273,18 @@ void paged_attention_batch(const PagedKVStorage& storage, const std::vector<cons
         detail::cuda_check(cudaStreamWaitEvent(nullptr, rt.side_done, 0), "order side work");
     }
     rt.finish("paged attention batch synchronize");
+}
+
+} // namespace
+
+void paged_attention_batch(const PagedKVStorage& storage, const std::vector<const SequenceState*>& sequences,
+                           const float* query_device, float* output_device, std::size_t query_heads) {
+    batch_decode(storage, sequences, query_device, output_device, query_heads, false);
+}
+
+void paged_attention_batch_host(const PagedKVStorage& storage, const std::vector<const SequenceState*>& sequences,
+                                const float* query_host, float* output_host, std::size_t query_heads) {
+    batch_decode(storage, sequences, query_host, output_host, query_heads, true);
 }
 
 } // namespace kvflux::v2

@@ -87,6 +87,11 @@ struct StorageRuntime {
     cudaEvent_t side_ready = nullptr;
     cudaEvent_t side_done = nullptr;
     void* ensure_workspace(std::size_t bytes);
+    // Device buffer for inputs staged from the caller's host memory (Q of
+    // paged_attention_batch_host); grows, never shrinks.
+    void* io = nullptr;
+    std::size_t io_bytes = 0;
+    void* ensure_io(std::size_t bytes);
     // Synchronises the legacy default stream and raises on device-side flags.
     void finish(const char* op) const;
 };

@@ -59,6 +59,7 @@ StorageRuntime::~StorageRuntime() {
     if (cudaSetDevice(device) != cudaSuccess) return;
     if (dev_scratch) (void)cudaFree(dev_scratch);
     if (workspace) (void)cudaFree(workspace);
+    if (io) (void)cudaFree(io);
     if (pinned) (void)cudaFreeHost(pinned);
     if (side_ready) (void)cudaEventDestroy(side_ready);
     if (side_done) (void)cudaEventDestroy(side_done);
@@ -141,6 +142,17 @@ void* StorageRuntime::ensure_workspace(std::size_t bytes) {
         workspace_bytes = bytes;
     }
     return workspace;
+}
+
+void* StorageRuntime::ensure_io(std::size_t bytes) {
+    if (bytes > io_bytes) {
+        if (io) cuda_check(cudaFree(io), "free input staging");
+        io = nullptr;
+        io_bytes = 0;
+        cuda_check(cudaMalloc(&io, bytes), "allocate input staging");
+        io_bytes = bytes;
+    }
+    return io;
 }
 
 void StorageRuntime::finish(const char* op) const {

@@ -227,6 +227,10 @@ PYBIND11_MODULE(_C, m) {
                                       py::object q, py::object o, std::size_t query_heads) {
         paged_attention_batch(s, seqs, ptr<const float>(q), ptr<float>(o), query_heads);
     });
+    m.def("paged_attention_batch_host", [](const PagedKVStorage& s, const std::vector<const SequenceState*>& seqs,
+                                           py::object q, py::object o, std::size_t query_heads) {
+        paged_attention_batch_host(s, seqs, ptr<const float>(q), ptr<float>(o), query_heads);
+    });
     m.def("append_token_cow", &append_token_cow);
     m.def("write_paged_kv_layers", [](const std::vector<PagedKVStorage*>& layers, py::object k, py::object v,
                                       const SlotMapping& slots) {
