@@ -543,7 +543,36 @@ class WriteGather:
         return (time.perf_counter() - t) * 1e3 / steps, 2 * kh.numel() * 2 + len(slots) * 8
 
 
-def layer_batches(kv, w, rank: int, world: int, ranks: Ranks, layers: int = 32) -> dict:
+def graph_ms(launch, ranks: Ranks, launches: int = 50, reps: int = 5) -> float:
+    """Per-launch device time of `launches` back-to-back launches captured in
+    one CUDA graph (max over ranks): the device rate without the host's
+    per-launch cost, for kernels about as short as a host launch."""
+    import torch
+
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        launch(s.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        for _ in range(launches):
+            launch(s.cuda_stream)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    ranks.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del graph
+    return ranks.reduce(e0.elapsed_time(e1) / (reps * launches), "max")
+
+
+def layer_batches(kv, w, rank: int, world: int, ranks: Ranks, layers: int = 32, steps: int = 50, warmup: int = 5,
+                  graph: bool = True) -> dict:
     """Config 2's step across a model's layers (Llama-3-8B: 32 layers, 8 KV
     heads x 128, bf16), one PagedKVStorage per layer on one odd/even
     fragmented pool of 8192 pages: 64 sequences of 1024 tokens. Write: the
@@ -588,32 +617,14 @@ def layer_batches(kv, w, rank: int, world: int, ranks: Ranks, layers: int = 32) 
         kv.check(kv.lib.kvfx_gather_layers(arr, layers, table_d.data_ptr(), lens_d.data_ptr(), nseq, width,
                                            kp.data_ptr(), vp.data_ptr(), per_layer, stream), "kvfx_gather_layers")
 
-    _, tot_w = time_launches(write, 50, 5, ranks)
-    _, tot_g = time_launches(gather, 10, 3, ranks)
-    # Back-to-back launches inside a CUDA graph: the device rate without the
-    # host's per-launch cost (a host launch takes about as long as this kernel).
-    s = torch.cuda.Stream()
-    with torch.cuda.stream(s):
-        write(s.cuda_stream)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=s):
-        for _ in range(50):
-            write(s.cuda_stream)
-    for _ in range(3):
-        graph.replay()
-    torch.cuda.synchronize()
-    ranks.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(5):
-        graph.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    del graph
-    wg_ms = ranks.reduce(e0.elapsed_time(e1) / 250, "max")
-    w_ms = ranks.reduce(tot_w / 50, "max")
-    g_ms = ranks.reduce(tot_g / 10, "max")
+    _, tot_w = time_launches(write, steps, warmup, ranks)
+    _, tot_g = time_launches(gather, max(1, steps // 5), 3, ranks)
+    wg_ms = float("nan")
+    if graph:
+        wg_ms = graph_ms(write, ranks)
+    w_ms = ranks.reduce(tot_w / steps, "max")
+    g_ms = ranks.reduce(tot_g / max(1, steps // 5), "max")
+
     peak = load_peak()[0]
     w_bytes = ranks.reduce(float(layers * (n * row * 2 * 2 + n * 8)), "sum")
     g_bytes = ranks.reduce(float(layers * nseq * total * row * 2 * 2 + table.nbytes), "sum")
@@ -622,8 +633,9 @@ def layer_batches(kv, w, rank: int, world: int, ranks: Ranks, layers: int = 32) 
            "write_tokens": n, "write_ms_per_launch": w_ms, "write_layer_tokens_per_s": layers * n / (w_ms * 1e-3),
            "write_gbs": w_bytes / (w_ms * 1e-3) / 1e9,
            "write_frac_of_peak": w_bytes / (w_ms * 1e-3) / 1e9 / (peak * world),
-           "write_graph_ms_per_launch": wg_ms, "write_graph_gbs": w_bytes / (wg_ms * 1e-3) / 1e9,
-           "write_graph_frac_of_peak": w_bytes / (wg_ms * 1e-3) / 1e9 / (peak * world),
+           "write_graph_ms_per_launch": wg_ms if graph else None,
+           "write_graph_gbs": w_bytes / (wg_ms * 1e-3) / 1e9 if graph else None,
+           "write_graph_frac_of_peak": w_bytes / (wg_ms * 1e-3) / 1e9 / (peak * world) if graph else None,
            "gather_ms_per_launch": g_ms, "gather_gbs": g_bytes / (g_ms * 1e-3) / 1e9,
            "gather_frac_of_peak": g_bytes / (g_ms * 1e-3) / 1e9 / (peak * world)}
     del stores, k_out, v_out
@@ -821,7 +833,8 @@ def only_case(args, ranks: Ranks, kv, w, peak: float) -> int:
         out = decode_step(kv, wl, args.steps, args.warmup, ranks)
         out.update({"case": args.only, "batch": cfg["batch"], "gbs": out["fused_kv_gbs"]})
     elif args.only == "layers":
-        out = layer_batches(kv, w, ranks.rank, ranks.world, ranks, layers=args.batch or 32)
+        out = layer_batches(kv, w, ranks.rank, ranks.world, ranks, layers=args.batch or 32, steps=args.steps,
+                            warmup=args.warmup, graph=args.steps >= 10)
         out.update({"case": args.only, "gbs": out["gather_gbs"]})
     elif args.only == "prefill4":
         pf = Prefill(kv, w, w.CONFIG4)
