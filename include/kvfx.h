@@ -218,6 +218,22 @@ const char* kvfx_last_error(void);
  */
 int kvfx_device_status(int device, uint32_t* flags, int clear);
 
+/*
+ * Self-test of device-side failure detection. Every kernel here that waits on
+ * a shared-memory barrier (TMA arrivals, tensor-core commits) bounds the wait
+ * (2 s): a wait that runs out raises KVFX_FLAG_TIMEOUT in the status word and
+ * the kernel returns instead of hanging; the C++ API then throws
+ * std::runtime_error. This call runs those waits (inline and out-of-line
+ * forms) on `device` on a barrier that nothing completes and nothing is in
+ * flight on, synchronously (~2 s). Returns KVFX_ETIMEOUT when both waits gave
+ * up and reported it (the expected outcome; the context stays usable),
+ * KVFX_EINVAL if a wait did not report it, KVFX_ECUDA on a CUDA error. The
+ * status word is left as it was (run no other work on the device meanwhile,
+ * or its timeout flag may be folded into the test's). No counterpart in the reference, whose
+ * kernels do not wait on barriers.
+ */
+int kvfx_selftest_wait_timeout(int device);
+
 /* Library version, e.g. "kvflux-b200 0.1.0 sm_100a". */
 const char* kvfx_version(void);
 

@@ -76,6 +76,7 @@ def _load():
     L.kvfx_last_error.restype = ctypes.c_char_p
     L.kvfx_last_error.argtypes = []
     L.kvfx_device_status.argtypes = [ctypes.c_int, ctypes.POINTER(u32), ctypes.c_int]
+    L.kvfx_selftest_wait_timeout.argtypes = [ctypes.c_int]
     L.kvfx_version.restype = ctypes.c_char_p
     L.kvfx_version.argtypes = []
     return L
@@ -88,7 +89,7 @@ KVFX_SYMBOLS = (
     "kvfx_write", "kvfx_gather", "kvfx_gather_batch", "kvfx_write_layers", "kvfx_gather_layers", "kvfx_copy_page", "kvfx_decode_workspace_bytes",
     "kvfx_decode_pages_per_split", "kvfx_decode", "kvfx_decode_append", "kvfx_decode_noalloc", "kvfx_attention_workspace_bytes",
     "kvfx_attention",
-    "kvfx_last_error", "kvfx_device_status", "kvfx_version",
+    "kvfx_last_error", "kvfx_device_status", "kvfx_selftest_wait_timeout", "kvfx_version",
 )
 
 DTYPE_CODE = {"float16": KVFX_F16, "bfloat16": KVFX_BF16, "float32": KVFX_F32}

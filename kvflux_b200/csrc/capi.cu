@@ -127,6 +127,26 @@ int kvfx_device_status(int device, uint32_t* flags, int clear) {
     return KVFX_OK;
 }
 
+int kvfx_selftest_wait_timeout(int device) {
+    if (device < 0) return fail(KVFX_EINVAL, "device ordinal must be non-negative");
+    DeviceScope scope(device);
+    if (scope.error() != cudaSuccess) return cuda_fail("select device", scope.error());
+    unsigned* st = status_word(device);
+    if (st == nullptr) return fail(KVFX_ECUDA, "status word unavailable on this device");
+    volatile unsigned* flags = st;
+    const unsigned before = *flags;
+    *flags = 0;
+    int completed[2] = {-1, -1};
+    const cudaError_t e = kvfx::launch_wait_selftest(st, nullptr, completed);
+    const unsigned seen = *flags;
+    *flags = before | (seen & ~KVFX_FLAG_TIMEOUT);  // the self-test's own flag is not left behind
+    if (e != cudaSuccess) return cuda_fail("wait self-test", e);
+    if (completed[0] != 0 || completed[1] != 0 || (seen & KVFX_FLAG_TIMEOUT) == 0) {
+        return fail(KVFX_EINVAL, "a bounded wait on an unsignalled barrier did not report a timeout");
+    }
+    return fail(KVFX_ETIMEOUT, "bounded device waits gave up on an unsignalled barrier and reported it");
+}
+
 int kvfx_write(const kvfx_cache* cache, const void* k_new, const void* v_new, const uint64_t* slots,
                uint64_t num_tokens, void* stream) {
     kvfx::CacheView c;

@@ -138,6 +138,10 @@ bool encode_cache_maps(const CacheView& c, CacheMaps* out, cudaError_t* err);
 // head_size 64/128, block 16, group <= 8 only).
 cudaError_t launch_decode_with_maps(const CacheView& c, const DecodeArgs& a, const CacheMaps& maps,
                                     unsigned* status, cudaStream_t s);
+// Runs the bounded-wait self-test kernel and waits for it; completed[w] = 1 if
+// warp w's wait completed, 0 if it gave up (the expected outcome).
+cudaError_t launch_wait_selftest(unsigned* status, cudaStream_t s, int* completed);
+
 // Records the calling thread's message for kvfx_last_error().
 void set_last_error(const char* msg);
 
