@@ -355,11 +355,12 @@ def e2e_decode(kv, wl: Decode, steps: int, warmup: int):
 def decode_step(kv, wl: Decode, steps: int, warmup: int, ranks: Ranks) -> dict:
     """Config 5 as a serving decode step: every sequence appends one token.
 
-    e2e: BatchDecodeSession.step (host page bookkeeping with copy-on-write,
-    16 bytes per row of lengths and slots uploaded, one fused write + decode
-    launch over the device-resident block table), with the step's new K/V
-    rows and Q copied from pinned host memory and O copied back, all inside
-    the timed region. Device: the fused launch alone, repeated on the state
+    e2e: BatchDecodeSession.step_host (host page bookkeeping with
+    copy-on-write, 16 bytes per row of lengths and slots uploaded, the step's
+    new K/V rows and Q uploaded from pinned host memory per row chunk, fused
+    write + decode launches over the device-resident block table writing O
+    into pinned host memory), all inside the timed region; beside it, step()
+    on device buffers with explicit copies before and after. Device: the fused launch alone, repeated on the state
     after the last step (it rewrites the same rows), next to a plain decode
     launch over the same table and lengths."""
     import torch
@@ -381,7 +382,7 @@ def decode_step(kv, wl: Decode, steps: int, warmup: int, ranks: Ranks) -> dict:
     o_host = torch.empty_like(q_host).pin_memory()
     sess = kv.BatchDecodeSession(wl.storage, seqs, wl.qh)
 
-    def step():
+    def step_device():
         k_dev.copy_(k_host, non_blocking=True)
         v_dev.copy_(v_host, non_blocking=True)
         wl.q.copy_(q_host, non_blocking=True)
@@ -389,20 +390,27 @@ def decode_step(kv, wl: Decode, steps: int, warmup: int, ranks: Ranks) -> dict:
         o_host.copy_(wl.o, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize()
-    ranks.barrier()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    wall = time.perf_counter()
-    t0.record()
-    for _ in range(steps):
-        step()
-    t1.record()
-    torch.cuda.synchronize()
-    wall = time.perf_counter() - wall
-    e2e_ms = max(t0.elapsed_time(t1), wall * 1e3) / steps
-    ranks.barrier()
+    def step_host():
+        sess.step_host(k_host, v_host, q_host, o_host)
+
+    def timed(step):
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        ranks.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        wall = time.perf_counter()
+        t0.record()
+        for _ in range(steps):
+            step()
+        t1.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - wall
+        ranks.barrier()
+        return max(t0.elapsed_time(t1), wall * 1e3) / steps
+
+    dev_api_ms = timed(step_device)
+    e2e_ms = timed(step_host)
 
     lens = np.array([s.num_tokens() for s in seqs], np.uint64)
     slots = np.array(kv.build_slot_mapping([(s, s.num_tokens() - 1) for s in seqs]), np.uint64)
@@ -432,6 +440,7 @@ def decode_step(kv, wl: Decode, steps: int, warmup: int, ranks: Ranks) -> dict:
     fused_ms = ranks.reduce(tot_f / steps, "max")
     plain_ms = ranks.reduce(tot_p / steps, "max")
     e2e_ms = ranks.reduce(e2e_ms, "max")
+    dev_api_ms = ranks.reduce(dev_api_ms, "max")
     kv_bytes = ranks.reduce(float(int(lens.sum()) * wl.kvh * wl.hd * 2 * 2), "sum")
     tokens = wl.batch
     world = ranks.world
@@ -441,7 +450,8 @@ def decode_step(kv, wl: Decode, steps: int, warmup: int, ranks: Ranks) -> dict:
             "e2e_kv_gbs": kv_bytes / (e2e_ms * 1e-3) / 1e9,
             "e2e_h2d_bytes_per_step": world * (2 * k_host.numel() * 2 + q_host.numel() * 4 + 2 * tokens * 8),
             "e2e_d2h_bytes_per_step": world * o_host.numel() * 4,
-            "api": "kvflux::v2::BatchDecodeSession::step",
+            "api": "kvflux::v2::BatchDecodeSession::step_host (pinned host K/V/Q in, O out)",
+            "device_api_ms_per_step": dev_api_ms,
             "fused_ms_per_launch": fused_ms, "fused_kv_gbs": kv_bytes / (fused_ms * 1e-3) / 1e9,
             "plain_decode_ms_per_launch": plain_ms, "table_width": width}
 

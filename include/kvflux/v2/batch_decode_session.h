@@ -42,6 +42,14 @@ public:
     std::vector<TokenLocation> step(const void* key_device, const void* value_device,
                                     const float* query_device, float* output_device);
 
+    // step() with key, value, query and output in page-locked host memory
+    // (cudaHostAlloc / cudaHostRegister): the inputs go up in two row chunks,
+    // each just ahead of its launch, and the launches write the output
+    // straight into the host buffer, so the transfers overlap the attention.
+    // Same results as step() on device copies of the same inputs.
+    std::vector<TokenLocation> step_host(const void* key_host, const void* value_host,
+                                         const float* query_host, float* output_host);
+
     // Re-reads row `row` (or every row) of the device table from its sequence.
     void refresh(std::size_t row);
     void refresh_all();

@@ -252,6 +252,9 @@ PYBIND11_MODULE(_C, m) {
         .def("step", [](BatchDecodeSession& b, py::object k, py::object v, py::object q, py::object o) {
             return b.step(ptr<const void>(k), ptr<const void>(v), ptr<const float>(q), ptr<float>(o));
         })
+        .def("step_host", [](BatchDecodeSession& b, py::object k, py::object v, py::object q, py::object o) {
+            return b.step_host(ptr<const void>(k), ptr<const void>(v), ptr<const float>(q), ptr<float>(o));
+        })
         .def("refresh", &BatchDecodeSession::refresh)
         .def("refresh_all", &BatchDecodeSession::refresh_all)
         .def("batch_size", &BatchDecodeSession::batch_size)

@@ -287,3 +287,43 @@ def test_batch_decode_session_argument_errors():
     with pytest.raises(ValueError):
         sess.step(np.zeros(512, np.uint8), x, x, x)    # host K
     assert a.num_tokens() == 5                        # nothing appended on a rejected call
+
+
+def test_batch_decode_session_step_host_matches_step():
+    """step_host (pinned host K/V/Q/O, two row chunks) gives the bits of
+    step() on device copies, on twin sessions built from the same seeds."""
+    kvh, hd, bs, group = 2, 128, 16, 4
+    qh = kvh * group
+    twins = [_Twin("bfloat16", kvh, hd, bs, capacity=4096, seed=41) for _ in range(2)]
+    batches = []
+    for t in twins:
+        seqs = []
+        for i in range(20):                      # >= 16 rows: the two-chunk path
+            s = kv.SequenceState(i + 1, t.pool)
+            t.prefill(s, 1 + 37 * i)
+            seqs.append(s)
+        seqs.append(t.fork(seqs[3], 99))         # a shared partial page: copy-on-write on the first step
+        batches.append(seqs)
+    sess = [kv.BatchDecodeSession(t.storage, b, qh) for t, b in zip(twins, batches)]
+    batch = len(batches[0])
+    for step in range(5):
+        k, v = twins[0].rand_rows(batch)
+        twins[1].rand_rows(batch)
+        q = w.normal(500 + step, batch * qh * hd)
+        o_dev = torch.empty(batch * qh * hd, device="cuda")
+        locs_d = sess[0].step(torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), torch.from_numpy(q).cuda(),
+                              o_dev)
+        kp, vp = torch.from_numpy(k).pin_memory(), torch.from_numpy(v).pin_memory()
+        qp, op = torch.from_numpy(q).pin_memory(), torch.full((batch * qh * hd,), 3.0).pin_memory()
+        locs_h = sess[1].step_host(kp, vp, qp, op)
+        assert [(a.physical_block, a.offset_in_block) for a in locs_d] == \
+            [(a.physical_block, a.offset_in_block) for a in locs_h]
+        assert np.array_equal(o_dev.cpu().numpy().view(np.uint32), op.numpy().view(np.uint32)), step
+        rb = kvh * hd * 2
+        for t in twins:
+            for r, s in enumerate(batches[twins.index(t)]):
+                t.rows[id(s)].append((k[r * rb:(r + 1) * rb], v[r * rb:(r + 1) * rb]))
+        err = float(np.abs(op.numpy() - twins[1].expected_out(batches[1], q, qh)).max())
+        assert err < 2e-3, (step, err)
+    with pytest.raises(ValueError):
+        sess[1].step_host(np.zeros(8, np.uint8), vp, qp, op)   # pageable K
