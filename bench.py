@@ -652,6 +652,59 @@ def layer_batches(kv, w, rank: int, world: int, ranks: Ranks, layers: int = 32, 
     return out
 
 
+def reference_gpu_sample(kv, w, rows: int = 4, reps: int = 3):
+    """The reference's own GPU kernels on this B200 beside this build's, on
+    the same sample: config 3's first `rows` requests (Llama-3-8B heads, bf16),
+    the same page ids and inputs, both driven through the v2 C++ API
+    (write_paged_kv of every token, then paged_attention_batch; synchronous
+    calls timed on the host clock, median of `reps`). None when the reference
+    GPU library is not built."""
+    import oracle
+    import torch
+
+    if oracle.ref_gpu() is None:
+        return None
+    cfg = w.CONFIG3
+    kvh, qh, hd, bs = cfg["kv_heads"], cfg["q_heads"], cfg["head_size"], cfg["block_size"]
+    lens = [int(x) for x in w.config_lengths(cfg)[:rows]]
+    nb = sum((l + bs - 1) // bs for l in lens) + 16
+    order = w.permutation(cfg["seed"], np.arange(nb))
+    total = sum(lens)
+    k = w.encode(w.normal(cfg["seed"] + 1, total * kvh * hd), "bfloat16")
+    v = w.encode(w.normal(cfg["seed"] + 2, total * kvh * hd), "bfloat16")
+    q = w.normal(cfg["seed"] + 3, rows * qh * hd)
+    o_ref, ref_write_ms, ref_ms = oracle.ref_gpu_decode(torch.cuda.current_device(), nb, bs, order, kvh, qh, hd, 1,
+                                                        lens, k, v, q, reps=reps)
+    pool = kv.PhysicalBlockPool(nb, bs)
+    w.fragment_pool(pool, order)
+    st = kv.PagedKVStorage(pool, kvh, hd, kv.DType.BFloat16, torch.cuda.current_device())
+    seqs = []
+    for L in lens:
+        s_ = kv.SequenceState(len(seqs) + 1, pool)
+        s_.append_tokens(L)
+        seqs.append(s_)
+    slots = kv.build_slot_mapping([(s_, t) for s_ in seqs for t in range(s_.num_tokens())])
+    kd, vd = torch.from_numpy(k.view(np.int16)).cuda(), torch.from_numpy(v.view(np.int16)).cuda()
+    t = time.perf_counter()
+    kv.write_paged_kv(st, kd, vd, slots)
+    write_ms = (time.perf_counter() - t) * 1e3
+    qd = torch.from_numpy(q).cuda()
+    o = torch.empty_like(qd)
+    times = []
+    for _ in range(reps + 2):
+        t = time.perf_counter()
+        kv.paged_attention_batch(st, seqs, qd, o, qh)
+        times.append((time.perf_counter() - t) * 1e3)
+    ours_ms = statistics.median(times[2:])
+    kv_bytes = total * kvh * hd * 2 * 2
+    return {"workload": f"config3 decode, requests 0-{rows - 1} (lengths {lens}), bf16; the reference's CUDA kernels "
+                        "(compiled from its sources for sm_100a) and this build's, both through the v2 C++ API",
+            "reference_decode_ms": ref_ms, "ours_decode_ms": ours_ms, "decode_speedup": ref_ms / ours_ms,
+            "reference_kv_gbs": kv_bytes / (ref_ms * 1e-3) / 1e9, "ours_kv_gbs": kv_bytes / (ours_ms * 1e-3) / 1e9,
+            "reference_write_ms": ref_write_ms, "ours_write_ms": write_ms, "write_tokens": total,
+            "max_abs_diff": float(np.abs(o.cpu().numpy() - o_ref).max())}
+
+
 class Prefill:
     """Config 4 on one GPU: 8 sequences x 4096 tokens, 32 Q / 8 KV heads,
     hd 128, bf16. Sequence 0 is written to 2056 tokens (128 full pages + a
@@ -842,6 +895,9 @@ def only_case(args, ranks: Ranks, kv, w, peak: float) -> int:
         wl = Decode(kv, w, cfg, ranks.rank, ranks.world)
         out = decode_step(kv, wl, args.steps, args.warmup, ranks)
         out.update({"case": args.only, "batch": cfg["batch"], "gbs": out["fused_kv_gbs"]})
+    elif args.only == "refgpu":
+        out = reference_gpu_sample(kv, w, rows=args.batch or 4, reps=args.steps) or {"reference_gpu": "not built"}
+        out.update({"case": args.only, "gbs": out.get("ours_kv_gbs", 0.0)})
     elif args.only == "layers":
         out = layer_batches(kv, w, ranks.rank, ranks.world, ranks, layers=args.batch or 32, steps=args.steps,
                             warmup=args.warmup, graph=args.steps >= 10)
@@ -883,7 +939,7 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="headline decode only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather", "prefill4", "step5", "layers"],
+    ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather", "prefill4", "step5", "layers", "refgpu"],
                     help="run one kernel's case alone (profiling runs); prints a short JSON line")
     ap.add_argument("--batch", type=int, default=None, help="override the batch: decode requests, write/gather sequences (profiling runs)")
     ap.add_argument("--shard", type=int, default=None,
@@ -995,6 +1051,9 @@ def main(argv=None) -> int:
         torch.cuda.empty_cache()
         secondary["layers_cfg2"] = layer_batches(kv, w, rank, world, ranks)
         torch.cuda.empty_cache()
+        if rank == 0 and world == 1:
+            secondary["reference_gpu_cfg3"] = reference_gpu_sample(kv, w)
+            torch.cuda.empty_cache()
         if rank == 0:
             pf = Prefill(kv, w, w.CONFIG4)
             per4, tot4 = time_launches(pf.launch, 3, 3, Ranks.this_rank_only())

@@ -203,3 +203,45 @@ def ref_decode_batch(k_cache, v_cache, dtype, kv_heads, bs, hd, table, lens, q_h
     _check(R.ref_decode_batch(_p(k_cache), _p(v_cache), dtype, kv_heads, bs, hd, _p(table), table.size // batch,
                               _p(lens), first, count, q_heads, _p(q), _p(out), threads), "ref_decode_batch")
     return out
+
+
+# ------------------------------------------------ reference GPU (compiled) ---
+
+_ref_gpu = None
+
+
+def ref_gpu():
+    """The reference's own GPU path (its CUDA kernels for sm_100a behind its
+    public API), or None if it was not built."""
+    global _ref_gpu
+    if _ref_gpu is None:
+        path = HERE / "_ref" / "libkvflux_ref_gpu.so"
+        if not path.exists():
+            return None
+        G = ctypes.CDLL(str(path))
+        G.kvref_gpu_decode.argtypes = [ctypes.c_int, u64, ctypes.c_uint32, vp, ctypes.c_uint32, ctypes.c_uint32,
+                                       ctypes.c_uint32, ctypes.c_uint32, vp, u64, vp, vp, vp, vp, ctypes.c_int,
+                                       ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
+        _ref_gpu = G
+    return _ref_gpu
+
+
+def ref_gpu_decode(device, num_blocks, block_size, page_order, kv_heads, q_heads, head_size, dtype, lens, k_rows,
+                   v_rows, q, reps=3):
+    """Batch decode through the reference's public GPU API (write_paged_kv of
+    every token, then paged_attention_batch `reps` times) on a pool whose free
+    list hands out `page_order`. Returns (O, write ms, median decode ms)."""
+    G = ref_gpu()
+    if G is None:
+        raise OracleError("reference GPU library not built")
+    page_order = np.ascontiguousarray(page_order, np.uint64)
+    lens = np.ascontiguousarray(lens, np.uint64)
+    k_rows = np.ascontiguousarray(k_rows)
+    v_rows = np.ascontiguousarray(v_rows)
+    q = np.ascontiguousarray(q, np.float32)
+    o = np.zeros(q.size, np.float32)
+    w_ms, d_ms = ctypes.c_double(0.0), ctypes.c_double(0.0)
+    _check(G.kvref_gpu_decode(device, num_blocks, block_size, _p(page_order), kv_heads, q_heads, head_size, dtype,
+                              _p(lens), len(lens), _p(k_rows), _p(v_rows), _p(q), _p(o), reps, ctypes.byref(w_ms),
+                              ctypes.byref(d_ms)), "kvref_gpu_decode")
+    return o, w_ms.value, d_ms.value

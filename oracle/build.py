@@ -8,6 +8,11 @@
                                  next to this repository in the build container).
                                  The built file travels with the tree; the
                                  sources are never copied into it.
+  oracle/_ref/libkvflux_ref_gpu.so - the reference's own GPU path (its CPU
+                                 control plane, v1 GpuMemoryPool, v2 storage and
+                                 its CUDA write/read/attention files) compiled
+                                 with nvcc for sm_100a + ref_gpu_shim.cpp: the
+                                 GPU-side baseline and an independent parity check.
 
 Usage: python oracle/build.py [--force]
 """
@@ -23,6 +28,18 @@ HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "libkvoracle.so"
 REF_DIR = HERE / "_ref"
 REF_LIB = REF_DIR / "libkvflux_ref.so"
+REF_GPU_LIB = REF_DIR / "libkvflux_ref_gpu.so"
+# The reference's GPU path on top of REF_SOURCES (its CMake target builds the
+# same files; src/v2/*.cu are its kernels).
+REF_GPU_EXTRA = [
+    "src/kv_layout.cpp",
+    "src/gpu_memory_pool.cpp",
+    "src/v2/paged_kv_storage.cpp",
+    "src/v2/copy_on_write.cpp",
+    "src/v2/paged_kv_write.cu",
+    "src/v2/paged_kv_read.cu",
+    "src/v2/paged_attention.cu",
+]
 REF_SOURCES = [
     "src/block_manager.cpp",
     "src/physical_block_pool.cpp",
@@ -66,8 +83,17 @@ def build(force: bool = False) -> dict:
             _run(["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-fvisibility=hidden", "-pthread",
                   f"-I{ref / 'include'}", *map(str, inputs), "-o", str(REF_LIB)])
         built["reference"] = str(REF_LIB)
+        gpu_inputs = [ref / s for s in REF_SOURCES + REF_GPU_EXTRA] + [HERE / "ref_gpu_shim.cpp"]
+        if force or _stale(REF_GPU_LIB, gpu_inputs):
+            nvcc = str(Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "bin" / "nvcc")
+            _run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-std=c++17", "-O2", "-shared",
+                  "-Xcompiler", "-fPIC,-fvisibility=hidden", "-cudart", "static", f"-I{ref / 'include'}",
+                  *map(str, gpu_inputs), "-o", str(REF_GPU_LIB)])
+        built["reference_gpu"] = str(REF_GPU_LIB)
     elif REF_LIB.exists():
         built["reference"] = str(REF_LIB)  # prebuilt elsewhere, shipped with the tree
+        if REF_GPU_LIB.exists():
+            built["reference_gpu"] = str(REF_GPU_LIB)
     return built
 
 
