@@ -653,7 +653,8 @@ def layer_batches(kv, w, rank: int, world: int, ranks: Ranks, layers: int = 32, 
 
 
 def reference_gpu_sample(kv, w, rows: int = 4, reps: int = 3):
-    """The reference's own GPU kernels on this B200 beside this build's, on
+    """Part of the baseline leg (rank 0, N = 1, not with --no-cpu).
+    The reference's own GPU kernels on this B200 beside this build's, on
     the same sample: config 3's first `rows` requests (Llama-3-8B heads, bf16),
     the same page ids and inputs, both driven through the v2 C++ API
     (write_paged_kv of every token, then paged_attention_batch; synchronous
@@ -895,9 +896,6 @@ def only_case(args, ranks: Ranks, kv, w, peak: float) -> int:
         wl = Decode(kv, w, cfg, ranks.rank, ranks.world)
         out = decode_step(kv, wl, args.steps, args.warmup, ranks)
         out.update({"case": args.only, "batch": cfg["batch"], "gbs": out["fused_kv_gbs"]})
-    elif args.only == "refgpu":
-        out = reference_gpu_sample(kv, w, rows=args.batch or 4, reps=args.steps) or {"reference_gpu": "not built"}
-        out.update({"case": args.only, "gbs": out.get("ours_kv_gbs", 0.0)})
     elif args.only == "layers":
         out = layer_batches(kv, w, ranks.rank, ranks.world, ranks, layers=args.batch or 32, steps=args.steps,
                             warmup=args.warmup, graph=args.steps >= 10)
@@ -939,7 +937,7 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="headline decode only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather", "prefill4", "step5", "layers", "refgpu"],
+    ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather", "prefill4", "step5", "layers"],
                     help="run one kernel's case alone (profiling runs); prints a short JSON line")
     ap.add_argument("--batch", type=int, default=None, help="override the batch: decode requests, write/gather sequences (profiling runs)")
     ap.add_argument("--shard", type=int, default=None,
@@ -1007,7 +1005,9 @@ def main(argv=None) -> int:
         err = float(np.abs(out[:count * wl.qh * wl.hd] - o_gpu[:count * wl.qh * wl.hd]).max())
         cpu = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": kind,
                "sample": f"{count} of config 5's 256 requests (gather + reference_attention), {secs:.1f} s",
-               "max_abs_err_vs_gpu": err}
+               "max_abs_err_vs_gpu": err,
+               # The reference's own GPU kernels on this box, beside this build's.
+               "reference_gpu_kernels": reference_gpu_sample(kv, w)}
 
     secondary = {}
     if not args.no_secondary:
@@ -1051,9 +1051,6 @@ def main(argv=None) -> int:
         torch.cuda.empty_cache()
         secondary["layers_cfg2"] = layer_batches(kv, w, rank, world, ranks)
         torch.cuda.empty_cache()
-        if rank == 0 and world == 1:
-            secondary["reference_gpu_cfg3"] = reference_gpu_sample(kv, w)
-            torch.cuda.empty_cache()
         if rank == 0:
             pf = Prefill(kv, w, w.CONFIG4)
             per4, tot4 = time_launches(pf.launch, 3, 3, Ranks.this_rank_only())
