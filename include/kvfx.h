@@ -162,7 +162,9 @@ int kvfx_decode(const kvfx_cache* cache, const float* q, float* o,
  * before that column are read as they are), and computes the same attention
  * as kvfx_decode over the updated rows; q, o, workspace and the other
  * arguments as for kvfx_decode. A slot outside the cache or at the wrong
- * offset is not written and sets KVFX_FLAG_BAD_INDEX.
+ * offset is not written and sets KVFX_FLAG_BAD_INDEX. Each new slot must lie
+ * in a page that no other row of the launch reads (copy a shared last page on
+ * write first, as append_token_cow does); rows' slots must be distinct.
  * Replaces, for a batch, the write_paged_kv + paged_attention pair of the
  * reference's decode step (KVFlux src/v2/sequence_lifecycle.cpp:53-73), with
  * the block table kept on the device instead of uploaded per call
