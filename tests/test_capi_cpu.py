@@ -75,3 +75,30 @@ def test_workspace_sizes():
     assert ws >= 64 * 8 * splits * 8 * 130 * 4
     # generic shapes need no workspace
     assert kv.lib.kvfx_decode_workspace_bytes(ctypes.byref(_cache(head_size=3)), 4, 4, 100, 0) == 0
+
+
+def test_new_entry_points_validate_before_cuda():
+    c = ctypes.byref(_cache())
+    # kvfx_decode_append: head ratio, null inputs, narrow table, empty batch
+    f = kv.lib.kvfx_decode_append
+    assert f(c, 1, 1, 1, 1, 1, 1, 1, 1, 1, 3, 10, 0, None, 0, None) == kv.KVFX_EINVAL   # 3 % 2 != 0
+    assert f(c, None, 1, 1, 1, 1, 1, 1, 1, 1, 4, 10, 0, None, 0, None) == kv.KVFX_EINVAL
+    assert f(c, 1, 1, 1, 1, 1, 1, 1, 1, 1, 4, 100, 0, None, 0, None) == kv.KVFX_EINVAL  # 1 block < 100 tokens
+    assert f(c, None, None, None, None, None, None, None, 0, 0, 4, 0, 0, None, 0, None) == kv.KVFX_OK
+    # layer batches: descriptors must agree, at most KVFX_MAX_LAYERS, strides cover a layer
+    two = (kv.KvfxCache * 2)(_cache(), _cache(k_base=16384, v_base=20480))
+    odd = (kv.KvfxCache * 2)(_cache(), _cache(head_size=16))
+    w_ = kv.lib.kvfx_write_layers
+    assert w_(None, 2, 1, 1, 1024, 1, 1, None) == kv.KVFX_EINVAL
+    assert w_(two, kv.KVFX_MAX_LAYERS + 1, 1, 1, 1024, 1, 1, None) == kv.KVFX_EINVAL
+    assert w_(odd, 2, 1, 1, 1024, 1, 1, None) == kv.KVFX_EINVAL
+    assert w_(two, 2, 1, 1, 16, 1, 1, None) == kv.KVFX_EINVAL                      # stride < 2 x 8 x 2 B x 1 token
+    assert w_(two, 2, None, None, 0, None, 0, None) == kv.KVFX_OK                  # no tokens
+    assert w_(two, 0, None, None, 0, None, 5, None) == kv.KVFX_OK                  # no layers
+    g = kv.lib.kvfx_gather_layers
+    assert g(odd, 2, 1, 1, 1, 1, 1, 1, 4096, None) == kv.KVFX_EINVAL
+    assert g(two, 2, None, 1, 1, 1, 1, 1, 4096, None) == kv.KVFX_EINVAL
+    assert g(two, 2, 1, 1, 70000, 1, 1, 1, 4096, None) == kv.KVFX_EINVAL          # batch above 65535
+    assert g(two, 2, None, None, 0, 0, None, None, 0, None) == kv.KVFX_OK
+    # the failure-detection self-test refuses a negative ordinal before CUDA
+    assert kv.lib.kvfx_selftest_wait_timeout(-1) == kv.KVFX_EINVAL
