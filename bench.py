@@ -766,6 +766,22 @@ class Prefill:
                                             t.data_ptr(), self.L, self.L, self.qh, None, 0, stream)
             self.kv.check(rc, "kvfx_attention")
 
+    def launch_batch(self, stream):
+        """The same 8 attentions as one kvfx_attention_batch call (one
+        persistent launch; each sequence has its own O buffer)."""
+        import torch
+
+        if not hasattr(self, "_batch"):
+            n = len(self.tables)
+            table = torch.stack(self.tables)
+            outs = [torch.empty_like(self.q) for _ in range(n)]
+            self._batch = (table, outs, (ctypes.c_void_p * n)(*[self.q.data_ptr()] * n),
+                           (ctypes.c_void_p * n)(*[o.data_ptr() for o in outs]), (ctypes.c_uint64 * n)(*[self.L] * n))
+        table, _, qp, op, lens = self._batch
+        rc = self.kv.lib.kvfx_attention_batch(ctypes.byref(self.desc), len(self.tables), qp, op, table.data_ptr(),
+                                              table.shape[1], lens, lens, self.qh, None, 0, stream)
+        self.kv.check(rc, "kvfx_attention_batch")
+
 
 # ----------------------------------------------------------- CPU baseline ---
 
@@ -902,9 +918,11 @@ def only_case(args, ranks: Ranks, kv, w, peak: float) -> int:
         out.update({"case": args.only, "gbs": out["gather_gbs"]})
     elif args.only == "prefill4":
         pf = Prefill(kv, w, w.CONFIG4)
-        per, total = time_launches(pf.launch, args.steps, args.warmup, ranks)
+        per, total = time_launches(pf.launch_batch, args.steps, args.warmup, ranks)
         ms = total / args.steps
-        out = {"case": args.only, "ms_per_step": ms, "launches_per_step": len(pf.tables),
+        per1, total1 = time_launches(pf.launch, args.steps, args.warmup, ranks)
+        out = {"case": args.only, "ms_per_step": ms, "launches_per_step": 1,
+               "per_sequence_calls_ms_per_step": total1 / args.steps,
                "tflops": pf.flops / (ms * 1e-3) / 1e12, "gbs": 0.0}
         out["frac_of_bf16_peak"] = out["tflops"] / load_bf16_peak()[0]
     else:
@@ -1053,13 +1071,15 @@ def main(argv=None) -> int:
         torch.cuda.empty_cache()
         if rank == 0:
             pf = Prefill(kv, w, w.CONFIG4)
-            per4, tot4 = time_launches(pf.launch, 3, 3, Ranks.this_rank_only())
+            per4, tot4 = time_launches(pf.launch_batch, 3, 3, Ranks.this_rank_only())
             ms4 = tot4 / 3
+            _, tot4s = time_launches(pf.launch, 3, 3, Ranks.this_rank_only())
             bf16_peak, bf16_kind = load_bf16_peak()
             secondary["prefill_cfg4"] = {
                 "workload": "config4 causal prefill: 8 x 4096 tokens, 32Q/8KV hd128 bf16, sequences 0-3 share 2056 "
                             "tokens (partial page copy-on-written), tcgen05 kernel",
-                "ms_per_step": ms4, "launches_per_step": len(pf.tables), "cow_page_copies": pf.cow_copies,
+                "ms_per_step": ms4, "launches_per_step": 1, "api": "kvfx_attention_batch",
+                "per_sequence_calls_ms_per_step": tot4s / 3, "cow_page_copies": pf.cow_copies,
                 "algorithmic_tflops": pf.flops / (ms4 * 1e-3) / 1e12,
                 "frac_of_bf16_peak": pf.flops / (ms4 * 1e-3) / 1e12 / bf16_peak, "peak_kind": bf16_kind,
                 "tensor_flops_executed_per_algorithmic": 2.0}

@@ -46,6 +46,9 @@ extern "C" {
 /* Most layers one kvfx_write_layers / kvfx_gather_layers call takes. */
 #define KVFX_MAX_LAYERS 128u
 
+/* Most sequences one kvfx_attention_batch call takes. */
+#define KVFX_MAX_PREFILL_SEQS 32u
+
 /* Bits of the per-device status word. */
 #define KVFX_FLAG_BAD_INDEX 1u  /* a slot/block id beyond the cache was skipped */
 #define KVFX_FLAG_TIMEOUT 2u    /* a bounded wait inside a kernel expired        */
@@ -209,6 +212,26 @@ uint64_t kvfx_attention_workspace_bytes(const kvfx_cache* cache, uint64_t query_
 int kvfx_attention(const kvfx_cache* cache, const float* q, float* o, const uint64_t* blocks,
                    uint64_t query_tokens, uint64_t kv_tokens, uint32_t q_heads,
                    void* workspace, uint64_t workspace_bytes, void* stream);
+
+/*
+ * kvfx_attention over num_seqs (<= KVFX_MAX_PREFILL_SEQS) sequences of one
+ * cache in one call: sequence i has query_tokens[i] queries aligned to the
+ * end of its kv_tokens[i] tokens, Q and O at the device addresses q[i] and
+ * o[i] (float[query_tokens[i]][q_heads][head_size]) and its pages in row i of
+ * the device table block_table[num_seqs][max_blocks_per_seq]. q, o,
+ * query_tokens and kv_tokens are host arrays of num_seqs entries. Each
+ * output equals what kvfx_attention gives for that sequence alone (bit for
+ * bit); the sequences of tensor-core prefill shapes run as one persistent
+ * launch that deals the query tiles of all of them, heaviest first, over the
+ * SMs, the others as one kvfx_attention each after it. The workspace is the largest
+ * kvfx_attention_workspace_bytes of the sequences. Sequences with no queries
+ * are skipped. Replaces the per-sequence loop over paged_attention's launch
+ * (KVFlux src/v2/paged_attention.cu:193-246) that a batched prefill makes.
+ */
+int kvfx_attention_batch(const kvfx_cache* cache, uint32_t num_seqs, const float* const* q, float* const* o,
+                         const uint64_t* block_table, uint64_t max_blocks_per_seq,
+                         const uint64_t* query_tokens, const uint64_t* kv_tokens, uint32_t q_heads,
+                         void* workspace, uint64_t workspace_bytes, void* stream);
 
 /* Message of the calling thread's last failed call ("" if none). */
 const char* kvfx_last_error(void);

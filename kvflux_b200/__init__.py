@@ -36,6 +36,7 @@ KVFX_OK, KVFX_EINVAL, KVFX_ERANGE, KVFX_EOVERFLOW, KVFX_ECUDA, KVFX_ETIMEOUT, KV
 KVFX_F16, KVFX_BF16, KVFX_F32 = 0, 1, 2
 KVFX_FLAG_BAD_INDEX, KVFX_FLAG_TIMEOUT = 1, 2
 KVFX_MAX_LAYERS = 128
+KVFX_MAX_PREFILL_SEQS = 32
 
 
 class KvfxCache(ctypes.Structure):
@@ -73,6 +74,7 @@ def _load():
     L.kvfx_attention_workspace_bytes.argtypes = [C, u64, u64, u32]
     L.kvfx_attention_workspace_bytes.restype = u64
     L.kvfx_attention.argtypes = [C, vp, vp, vp, u64, u64, u32, vp, u64, vp]
+    L.kvfx_attention_batch.argtypes = [C, u32, vp, vp, vp, u64, vp, vp, u32, vp, u64, vp]
     L.kvfx_last_error.restype = ctypes.c_char_p
     L.kvfx_last_error.argtypes = []
     L.kvfx_device_status.argtypes = [ctypes.c_int, ctypes.POINTER(u32), ctypes.c_int]
@@ -88,7 +90,7 @@ lib = _load()
 KVFX_SYMBOLS = (
     "kvfx_write", "kvfx_gather", "kvfx_gather_batch", "kvfx_write_layers", "kvfx_gather_layers", "kvfx_copy_page", "kvfx_decode_workspace_bytes",
     "kvfx_decode_pages_per_split", "kvfx_decode", "kvfx_decode_append", "kvfx_decode_noalloc", "kvfx_attention_workspace_bytes",
-    "kvfx_attention",
+    "kvfx_attention", "kvfx_attention_batch",
     "kvfx_last_error", "kvfx_device_status", "kvfx_selftest_wait_timeout", "kvfx_version",
 )
 

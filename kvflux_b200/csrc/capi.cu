@@ -2,6 +2,7 @@
 // and dispatch to the kernel launchers. No entry point allocates device
 // memory per call; the only allocation is the per-device status word (one
 // mapped host word, made on a device's first call).
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <limits>
@@ -433,6 +434,63 @@ int kvfx_attention(const kvfx_cache* cache, const float* q, float* o, const uint
     kvfx::AttentionArgs a{q, o, blocks, query_tokens, kv_tokens, q_heads, workspace, workspace_bytes};
     const cudaError_t e = kvfx::launch_attention(c, a, status_word(c.device), static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? KVFX_OK : cuda_fail("paged attention launch", e);
+}
+
+int kvfx_attention_batch(const kvfx_cache* cache, uint32_t num_seqs, const float* const* q, float* const* o,
+                         const uint64_t* block_table, uint64_t max_blocks_per_seq,
+                         const uint64_t* query_tokens, const uint64_t* kv_tokens, uint32_t q_heads,
+                         void* workspace, uint64_t workspace_bytes, void* stream) {
+    kvfx::CacheView c;
+    if (int rc = make_view(cache, &c); rc != KVFX_OK) return rc;
+    if (num_seqs > KVFX_MAX_PREFILL_SEQS) return fail(KVFX_EINVAL, "more sequences than KVFX_MAX_PREFILL_SEQS");
+    if (num_seqs == 0) return KVFX_OK;
+    if (q == nullptr || o == nullptr || query_tokens == nullptr || kv_tokens == nullptr) {
+        return fail(KVFX_EINVAL, "q, o, query_tokens and kv_tokens must be non-null");
+    }
+    if (q_heads == 0 || q_heads % c.heads != 0) return fail(KVFX_EINVAL, "invalid attention shape");
+    kvfx::AttentionArgs seqs[KVFX_MAX_PREFILL_SEQS];
+    uint32_t n = 0;
+    uint64_t need = 0;
+    for (uint32_t i = 0; i < num_seqs; ++i) {
+        const uint64_t qt = query_tokens[i], kt = kv_tokens[i];
+        if (qt > kt) return fail(KVFX_EINVAL, "invalid attention shape");
+        if (qt == 0) continue;
+        if (block_table == nullptr || q[i] == nullptr || o[i] == nullptr) {
+            return fail(KVFX_EINVAL, "q, o and block_table must be non-null");
+        }
+        if (kvfx::ceil_div(kt, c.bs) > max_blocks_per_seq) {
+            return fail(KVFX_EINVAL, "a sequence needs more pages than max_blocks_per_seq");
+        }
+        uint64_t elems = 0, tmp = 0;
+        if (!mul_ok(qt, q_heads, &tmp) || !mul_ok(tmp, c.hd, &elems)) {
+            return fail(KVFX_EOVERFLOW, "query size overflows");
+        }
+        if (!mul_ok(i, max_blocks_per_seq, &tmp)) return fail(KVFX_EOVERFLOW, "block table size overflows");
+        seqs[n] = kvfx::AttentionArgs{q[i], o[i], block_table + tmp, qt, kt, q_heads, workspace, workspace_bytes};
+        need = std::max(need, kvfx::attention_workspace_bytes(c, qt, kt, q_heads));
+        ++n;
+    }
+    // Tensor-core shapes first (stable order), the rest after them.
+    const auto tc_end = std::stable_partition(seqs, seqs + n, [&](const kvfx::AttentionArgs& a) {
+        return kvfx::prefill_tc_supported(c, a);
+    });
+    const uint32_t n_tc = static_cast<uint32_t>(tc_end - seqs);
+    if (n == 0) return KVFX_OK;
+    if (need != 0 && (workspace == nullptr || workspace_bytes < need)) {
+        return fail(KVFX_ENOSPACE, "attention workspace is smaller than the largest kvfx_attention_workspace_bytes()");
+    }
+    DeviceScope scope(c.device);
+    if (scope.error() != cudaSuccess) return cuda_fail("select device", scope.error());
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (n_tc != 0) {
+        const cudaError_t e = kvfx::launch_prefill_tc_batch(c, seqs, n_tc, status_word(c.device), s);
+        if (e != cudaSuccess) return cuda_fail("batched prefill launch", e);
+    }
+    for (uint32_t i = n_tc; i < n; ++i) {
+        const cudaError_t e = kvfx::launch_attention(c, seqs[i], status_word(c.device), s);
+        if (e != cudaSuccess) return cuda_fail("paged attention launch", e);
+    }
+    return KVFX_OK;
 }
 
 }  // extern "C"

@@ -108,6 +108,10 @@ cudaError_t launch_attention(const CacheView& c, const AttentionArgs& a, unsigne
 // Causal prefill on tcgen05 (prefill.cu): shapes it covers, and the launch.
 bool prefill_tc_supported(const CacheView& c, const AttentionArgs& a);
 cudaError_t launch_prefill_tc(const CacheView& c, const AttentionArgs& a, unsigned* status, cudaStream_t s);
+// Several sequences (each prefill_tc_supported, one q_heads) in one
+// persistent launch; at most KVFX_MAX_PREFILL_SEQS.
+cudaError_t launch_prefill_tc_batch(const CacheView& c, const AttentionArgs* seqs, uint32_t n, unsigned* status,
+                                    cudaStream_t s);
 
 // Generic SIMT attention over "query rows" (used by both entry points for the
 // shapes the specialised kernels do not cover).

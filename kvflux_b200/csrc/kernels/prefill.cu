@@ -35,6 +35,7 @@
 //
 // Semantics: KVFlux src/v2/paged_attention.cu:109-128 (query i sees
 // positions <= kv_tokens - query_tokens + i; KV head = q_head / group).
+#include <algorithm>
 #include <cmath>
 #include <type_traits>
 
@@ -48,6 +49,7 @@ namespace {
 constexpr int kBM = 128;         // query rows per unit
 constexpr int kBN = 128;         // KV tokens per tile (8 pages of 16)
 constexpr int kHD = 128;         // head size handled here
+constexpr uint32_t kMaxPrefillSeqs = KVFX_MAX_PREFILL_SEQS;  // sequences per launch
 constexpr int kKStages = 3;      // K ring depth
 constexpr int kVStages = 2;      // V ring depth
 constexpr int kSBufs = 3;        // S/P buffers in TMEM
@@ -69,35 +71,55 @@ constexpr uint32_t kOffV = kOffK + kKStages * kKVTile;
 constexpr uint32_t kSmemBytes = kOffV + kVStages * kKVTile;   // 224 KiB
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
 
-struct PrefillParams {
+// One sequence of a launch: its Q and O ([q_tokens][q_heads][128] FP32), its
+// page ids and its lengths.
+struct PrefillSeq {
     const float* q;
     float* o;
     const uint64_t* blocks;
-    uint64_t q_tokens, kv_tokens, num_blocks, n_units;
-    uint32_t q_heads, kv_heads, group, n_qtiles;
+    uint64_t q_tokens, kv_tokens;
+};
+
+struct PrefillParams {
+    PrefillSeq seq[kMaxPrefillSeqs];
+    uint64_t num_blocks, n_units;  // n_units: max query tiles x sequences x Q heads (shorter sequences leave gaps)
+    uint32_t num_seqs, q_heads, kv_heads, group;
     float qscale;
     unsigned* status;
 };
 
 struct Unit {
     uint64_t q0;
-    uint32_t qh, kh, ntiles;
+    uint32_t qh, kh, ntiles, s;
 };
 
-// The unit this CTA takes in round `round` (false when it has none left).
-__device__ __forceinline__ bool unit_at(const PrefillParams& p, uint32_t round, Unit& u) {
+// The unit this CTA takes in dealing round `round` (false when it has none
+// left). Unit index = (unit round, sequence, Q head); unit round 0 holds
+// every sequence's last query tile, so the heaviest units come first across
+// sequences; an index past a shorter sequence's first tile is a gap, and the
+// CTA moves on to its next round (every role calls this with its own round
+// counter and skips the same gaps).
+__device__ __forceinline__ bool unit_at(const PrefillParams& p, uint32_t& round, Unit& u) {
     const uint64_t G = gridDim.x;
-    const uint64_t base = static_cast<uint64_t>(round) * G;
-    if (base >= p.n_units) return false;
-    const uint64_t idx = base + ((round & 1u) ? (G - 1 - blockIdx.x) : blockIdx.x);
-    if (idx >= p.n_units) return false;  // partial last round
-    const uint32_t qtile = p.n_qtiles - 1 - static_cast<uint32_t>(idx / p.q_heads);
-    u.qh = static_cast<uint32_t>(idx % p.q_heads);
-    u.kh = u.qh / p.group;
-    u.q0 = static_cast<uint64_t>(qtile) * kBM;
-    const uint64_t q_last = umin64(u.q0 + kBM, p.q_tokens) - 1;
-    u.ntiles = static_cast<uint32_t>((p.kv_tokens - p.q_tokens + q_last) / kBN + 1);
-    return true;
+    for (;; ++round) {
+        const uint64_t base = static_cast<uint64_t>(round) * G;
+        if (base >= p.n_units) return false;
+        const uint64_t idx = base + ((round & 1u) ? (G - 1 - blockIdx.x) : blockIdx.x);
+        if (idx >= p.n_units) return false;  // partial last round
+        const uint64_t per_round = static_cast<uint64_t>(p.num_seqs) * p.q_heads;
+        const uint64_t ur = idx / per_round;
+        const uint32_t rem = static_cast<uint32_t>(idx - ur * per_round);
+        u.s = rem / p.q_heads;
+        u.qh = rem - u.s * p.q_heads;
+        const PrefillSeq& sq = p.seq[u.s];
+        const uint64_t nq = ceil_div(sq.q_tokens, kBM);
+        if (ur >= nq) continue;
+        u.kh = u.qh / p.group;
+        u.q0 = (nq - 1 - ur) * kBM;
+        const uint64_t q_last = umin64(u.q0 + kBM, sq.q_tokens) - 1;
+        u.ntiles = static_cast<uint32_t>((sq.kv_tokens - sq.q_tokens + q_last) / kBN + 1);
+        return true;
+    }
 }
 
 // Position in this CTA's stream of KV tiles: unit ordinal k, tile j of the
@@ -108,14 +130,15 @@ struct TileCursor {
     bool valid;
     __device__ __forceinline__ void init(const PrefillParams& p) {
         round = k = j = g = 0;
-        valid = unit_at(p, 0, u);
+        valid = unit_at(p, round, u);
     }
     __device__ __forceinline__ void next(const PrefillParams& p) {
         ++g;
         if (++j < u.ntiles) return;
         j = 0;
         ++k;
-        valid = unit_at(p, ++round, u);
+        ++round;
+        valid = unit_at(p, round, u);
     }
     __device__ __forceinline__ bool last() const { return j + 1 == u.ntiles; }
 };
@@ -139,12 +162,14 @@ __device__ __forceinline__ uint32_t swz_row(uint32_t r, uint32_t c) {
     return (r >> 3) * 1024 + (r & 7) * 128 + (((c ^ r) & 7) << 4);
 }
 
-// Page id of page `lane` of KV tile j in lanes 0..7 (one load per lane, all
-// in one memory round trip); 0 in the other lanes.
-__device__ __forceinline__ uint64_t tile_page_id(const PrefillParams& p, uint32_t j, uint64_t npages, uint32_t lane) {
+// Page id of page `lane` of KV tile j of sequence s in lanes 0..7 (one load
+// per lane, all in one memory round trip); 0 in the other lanes.
+__device__ __forceinline__ uint64_t tile_page_id(const PrefillParams& p, uint32_t s, uint32_t j, uint32_t lane) {
     if (lane >= kBN / 16) return 0;
+    const PrefillSeq& sq = p.seq[s];
+    const uint64_t npages = ceil_div(sq.kv_tokens, 16);
     const uint64_t lp = static_cast<uint64_t>(j) * (kBN / 16) + lane;
-    return __ldg(p.blocks + (lp < npages ? lp : 0));
+    return __ldg(sq.blocks + (lp < npages ? lp : 0));
 }
 
 // One KV tile (8 pages of one KV head) into a ring slot. Warp-wide: page pg's
@@ -180,7 +205,7 @@ __device__ __forceinline__ void load_kv_tile(const PrefillParams& p, const CUten
 // The next tile's page ids are fetched while waiting for its slot. At the
 // end, waits for its own copies in flight.
 __device__ __noinline__ void produce(const PrefillParams& p, const CUtensorMap* map, unsigned char* ring,
-                                     uint64_t* full, uint64_t* done, uint64_t npages, uint32_t kStages) {
+                                     uint64_t* full, uint64_t* done, uint32_t kStages) {
     const uint32_t lane = threadIdx.x & 31u;
     const bool leader = elect_one();
     auto wait = [&](uint64_t* bar, uint32_t phase) {
@@ -189,7 +214,7 @@ __device__ __noinline__ void produce(const PrefillParams& p, const CUtensorMap* 
     if (leader) prefetch_tensormap(map);
     TileCursor c;
     c.init(p);
-    uint64_t id = c.valid ? tile_page_id(p, c.j, npages, lane) : 0;
+    uint64_t id = c.valid ? tile_page_id(p, c.u.s, c.j, lane) : 0;
     uint32_t issued = 0;
     while (c.valid) {
         const uint32_t g = c.g, st = g % kStages;
@@ -200,7 +225,7 @@ __device__ __noinline__ void produce(const PrefillParams& p, const CUtensorMap* 
         load_kv_tile(p, map, ring + st * kKVTile, c.u.kh, id, leader, &full[st]);
         issued = g + 1;
         c.next(p);
-        if (c.valid) id = tile_page_id(p, c.j, npages, lane);
+        if (c.valid) id = tile_page_id(p, c.u.s, c.j, lane);
     }
     for (uint32_t g = issued > kStages ? issued - kStages : 0; g < issued; ++g)
         (void)wait(&full[g % kStages], (g / kStages) & 1u);
@@ -220,7 +245,6 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_addr(smem);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint64_t npages = ceil_div(p.kv_tokens, 16);
 
     if (tid == 0) {
         for (int s = 0; s < kKStages; ++s) mbar_init(&k_full[s], 1);
@@ -248,10 +272,10 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
 
     if (warp == 0) {
         // ---------------------------------------------------- K producer ---
-        produce(p, &kmap, smem + kOffK, k_full, s_full, npages, kKStages);
+        produce(p, &kmap, smem + kOffK, k_full, s_full, kKStages);
     } else if (warp == 2) {
         // ---------------------------------------------------- V producer ---
-        produce(p, &vmap, smem + kOffV, v_full, pv_done, npages, kVStages);
+        produce(p, &vmap, smem + kOffV, v_full, pv_done, kVStages);
     } else if (warp == 1) {
         // ----------------------------------------------------- MMA issuer ---
         // The whole warp runs the schedule (its values stay warp-uniform);
@@ -402,7 +426,8 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
         Unit u;
         for (uint32_t round = 0, k = 0; ok && unit_at(p, round, u); ++round, ++k) {
             // Last visible position of this row.
-            const int64_t pos = static_cast<int64_t>(p.kv_tokens - p.q_tokens + u.q0 + r);
+            const PrefillSeq& sq = p.seq[u.s];
+            const int64_t pos = static_cast<int64_t>(sq.kv_tokens - sq.q_tokens + u.q0 + r);
             float m_run = -INFINITY, l_run = 0.f;
             for (uint32_t j = 0; j < u.ntiles; ++j, ++g) {
                 const uint32_t b = g % kSBufs;
@@ -529,10 +554,10 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
                 // (unwritten slots may hold NaN; 0 * NaN must not reach O).
                 // Done before P(g) is published, which precedes PV(g).
                 const uint64_t t0 = static_cast<uint64_t>(j) * kBN;
-                if (t0 + kBN > p.kv_tokens) {
+                if (t0 + kBN > sq.kv_tokens) {
                     const uint32_t sv = g % kVStages;
                     if (!wait_all(&v_full[sv], (g / kVStages) & 1u)) { ok = false; break; }
-                    const uint32_t valid = static_cast<uint32_t>(p.kv_tokens - t0);
+                    const uint32_t valid = static_cast<uint32_t>(sq.kv_tokens - t0);
                     const uint32_t rows = kBN - valid;
                     unsigned char* vt = smem + kOffV + sv * kKVTile;
                     for (uint32_t i = r; i < rows * 2 * 8; i += 128) {
@@ -551,8 +576,8 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
             tc::fence_after_sync();
             const float inv = 1.f / l_run;
             const uint64_t qi = u.q0 + r;
-            const bool row_live = qi < p.q_tokens;
-            float* orow = p.o + (qi * p.q_heads + u.qh) * kHD;
+            const bool row_live = qi < sq.q_tokens;
+            float* orow = sq.o + (qi * p.q_heads + u.qh) * kHD;
 #pragma unroll 1
             for (int cb = 0; cb < kHD; cb += 32) {
                 float ov[32];
@@ -577,10 +602,11 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
         Unit u;
         for (uint32_t round = 0, k = 0; unit_at(p, round, u); ++round, ++k) {
             const uint64_t qi = u.q0 + r;
-            const bool row_live = qi < p.q_tokens;
+            const PrefillSeq& sq = p.seq[u.s];
+            const bool row_live = qi < sq.q_tokens;
             float v[kHD];
             if (row_live) {
-                const float4* qrow = reinterpret_cast<const float4*>(p.q + (qi * p.q_heads + u.qh) * kHD);
+                const float4* qrow = reinterpret_cast<const float4*>(sq.q + (qi * p.q_heads + u.qh) * kHD);
 #pragma unroll
                 for (int e = 0; e < kHD / 4; ++e) {
                     const float4 x = __ldg(qrow + e);
@@ -629,7 +655,10 @@ bool prefill_eligible(const CacheView& c, const AttentionArgs& a) {
 
 bool prefill_tc_supported(const CacheView& c, const AttentionArgs& a) { return prefill_eligible(c, a); }
 
-cudaError_t launch_prefill_tc(const CacheView& c, const AttentionArgs& a, unsigned* status, cudaStream_t s) {
+cudaError_t launch_prefill_tc_batch(const CacheView& c, const AttentionArgs* seqs, uint32_t n, unsigned* status,
+                                    cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    if (n > kMaxPrefillSeqs) return cudaErrorInvalidValue;
     cudaError_t err = cudaSuccess;
     const CacheMaps* maps = cache_maps(c, &err);
     if (maps == nullptr) return err != cudaSuccess ? err : cudaErrorInvalidValue;
@@ -646,18 +675,18 @@ cudaError_t launch_prefill_tc(const CacheView& c, const AttentionArgs& a, unsign
     }
     const int sms = device_sm_count(c.device);
     if (sms <= 0) return cudaErrorInvalidDevice;
-    PrefillParams p;
-    p.q = a.q;
-    p.o = a.o;
-    p.blocks = a.blocks;
-    p.q_tokens = a.query_tokens;
-    p.kv_tokens = a.kv_tokens;
+    PrefillParams p{};
+    uint64_t max_qtiles = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        p.seq[i] = PrefillSeq{seqs[i].q, seqs[i].o, seqs[i].blocks, seqs[i].query_tokens, seqs[i].kv_tokens};
+        max_qtiles = std::max<uint64_t>(max_qtiles, ceil_div(seqs[i].query_tokens, kBM));
+    }
+    p.num_seqs = n;
     p.num_blocks = c.num_blocks;
-    p.q_heads = a.q_heads;
+    p.q_heads = seqs[0].q_heads;
     p.kv_heads = c.heads;
-    p.group = a.q_heads / c.heads;
-    p.n_qtiles = static_cast<uint32_t>(ceil_div(a.query_tokens, kBM));
-    p.n_units = static_cast<uint64_t>(p.n_qtiles) * a.q_heads;
+    p.group = p.q_heads / c.heads;
+    p.n_units = max_qtiles * n * p.q_heads;
     p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.hd)));
     p.status = status;
     const unsigned grid = static_cast<unsigned>(umin64(p.n_units, static_cast<uint64_t>(sms)));
@@ -667,6 +696,10 @@ cudaError_t launch_prefill_tc(const CacheView& c, const AttentionArgs& a, unsign
         prefill_tc_kernel<__half><<<grid, kThreads, kSmemAlloc, s>>>(p, maps->k, maps->v);
     }
     return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_tc(const CacheView& c, const AttentionArgs& a, unsigned* status, cudaStream_t s) {
+    return launch_prefill_tc_batch(c, &a, 1, status, s);
 }
 
 }  // namespace kvfx
