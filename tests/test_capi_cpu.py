@@ -100,5 +100,20 @@ def test_new_entry_points_validate_before_cuda():
     assert g(two, 2, None, 1, 1, 1, 1, 1, 4096, None) == kv.KVFX_EINVAL
     assert g(two, 2, 1, 1, 70000, 1, 1, 1, 4096, None) == kv.KVFX_EINVAL          # batch above 65535
     assert g(two, 2, None, None, 0, 0, None, None, 0, None) == kv.KVFX_OK
+    # batched attention: sequence count, head ratio, shapes, table width, null arrays
+    a = kv.lib.kvfx_attention_batch
+    n = kv.KVFX_MAX_PREFILL_SEQS + 1
+    ptrs = (ctypes.c_void_p * n)(*[64] * n)
+    ones = (ctypes.c_uint64 * n)(*[4] * n)
+    assert a(c, n, ptrs, ptrs, 1, 1, ones, ones, 4, None, 0, None) == kv.KVFX_EINVAL
+    assert a(c, 2, ptrs, ptrs, 1, 1, ones, ones, 3, None, 0, None) == kv.KVFX_EINVAL      # 3 % 2 != 0
+    qt, kt = (ctypes.c_uint64 * 2)(4, 9), (ctypes.c_uint64 * 2)(4, 8)
+    assert a(c, 2, ptrs, ptrs, 1, 1, qt, kt, 4, None, 0, None) == kv.KVFX_EINVAL         # 9 queries > 8 tokens
+    kt2 = (ctypes.c_uint64 * 2)(4, 40)
+    assert a(c, 2, ptrs, ptrs, 1, 2, qt, kt2, 4, None, 0, None) == kv.KVFX_EINVAL        # 40 tokens > 2 blocks of 16
+    assert a(c, 2, None, ptrs, 1, 1, ones, ones, 4, None, 0, None) == kv.KVFX_EINVAL
+    zero = (ctypes.c_uint64 * 2)(0, 0)
+    assert a(c, 2, ptrs, ptrs, None, 0, zero, kt, 4, None, 0, None) == kv.KVFX_OK         # no queries
+    assert a(c, 0, None, None, None, 0, None, None, 4, None, 0, None) == kv.KVFX_OK
     # the failure-detection self-test refuses a negative ordinal before CUDA
     assert kv.lib.kvfx_selftest_wait_timeout(-1) == kv.KVFX_EINVAL
