@@ -795,7 +795,8 @@ def cpu_threads() -> int:
 def cpu_decode_sample(hk, hv, nb, kvh, bs, hd, table, lens, qh, q, budget_s: float = 15.0):
     """Times the reference CPU path (gather + reference_attention per request,
     one std::thread per request slice) on the sample; returns
-    (KV GB/s, seconds, kind, threads, requests used, outputs)."""
+    (KV GB/s, seconds, kind, threads, requests used, outputs, single-core KV
+    GB/s of the one-request calibration run)."""
     import oracle
 
     threads = cpu_threads()
@@ -820,7 +821,8 @@ def cpu_decode_sample(hk, hv, nb, kvh, bs, hd, table, lens, qh, q, budget_s: flo
     count = min(len(lens), max(1, waves * threads))
     secs, out = run(count)
     kv_bytes = int(lens[:count].sum()) * kvh * hd * 2 * 2
-    return kv_bytes / secs / 1e9, secs, "reference" if use_ref else "port", min(threads, count), count, out
+    one_core = int(lens[0]) * kvh * hd * 2 * 2 / max(t1, 1e-9) / 1e9
+    return kv_bytes / secs / 1e9, secs, "reference" if use_ref else "port", min(threads, count), count, out, one_core
 
 
 # ------------------------------------------------------------- reference ---
@@ -1019,11 +1021,14 @@ def main(argv=None) -> int:
     if rank == 0 and world == 1 and not args.no_cpu:
         sample_req = list(range(min(16, wl.batch)))
         hk, hv, nb, table, lens, q, o_gpu = wl.host_sample(sample_req)
-        gbs, secs, kind, cores, count, out = cpu_decode_sample(hk, hv, nb, wl.kvh, wl.bs, wl.hd, table, lens, wl.qh, q)
+        gbs, secs, kind, cores, count, out, one_core = cpu_decode_sample(hk, hv, nb, wl.kvh, wl.bs, wl.hd, table,
+                                                                         lens, wl.qh, q)
         err = float(np.abs(out[:count * wl.qh * wl.hd] - o_gpu[:count * wl.qh * wl.hd]).max())
         cpu = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": kind,
                "sample": f"{count} of config 5's 256 requests (gather + reference_attention), {secs:.1f} s",
                "max_abs_err_vs_gpu": err,
+               "single_core": {"value": one_core, "unit": "GB/s", "cores": 1,
+                               "sample": "request 0 alone, the same code on one thread"},
                # The reference's own GPU kernels on this box, beside this build's.
                "reference_gpu_kernels": reference_gpu_sample(kv, w)}
 
