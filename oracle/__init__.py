@@ -230,7 +230,8 @@ def ref_gpu_decode(device, num_blocks, block_size, page_order, kv_heads, q_heads
                    v_rows, q, reps=3):
     """Batch decode through the reference's public GPU API (write_paged_kv of
     every token, then paged_attention_batch `reps` times) on a pool whose free
-    list hands out `page_order`. Returns (O, write ms, median decode ms)."""
+    list hands out `page_order`. Returns (O, (first write ms, median ms of
+    `reps` repeated writes), median decode ms)."""
     G = ref_gpu()
     if G is None:
         raise OracleError("reference GPU library not built")
@@ -240,8 +241,8 @@ def ref_gpu_decode(device, num_blocks, block_size, page_order, kv_heads, q_heads
     v_rows = np.ascontiguousarray(v_rows)
     q = np.ascontiguousarray(q, np.float32)
     o = np.zeros(q.size, np.float32)
-    w_ms, d_ms = ctypes.c_double(0.0), ctypes.c_double(0.0)
+    w_ms, d_ms = (ctypes.c_double * 2)(0.0, 0.0), ctypes.c_double(0.0)
     _check(G.kvref_gpu_decode(device, num_blocks, block_size, _p(page_order), kv_heads, q_heads, head_size, dtype,
-                              _p(lens), len(lens), _p(k_rows), _p(v_rows), _p(q), _p(o), reps, ctypes.byref(w_ms),
+                              _p(lens), len(lens), _p(k_rows), _p(v_rows), _p(q), _p(o), reps, w_ms,
                               ctypes.byref(d_ms)), "kvref_gpu_decode")
-    return o, w_ms.value, d_ms.value
+    return o, (w_ms[0], w_ms[1]), d_ms.value
