@@ -479,10 +479,22 @@ class WriteGather:
                                                         for p in range(pre, pre + new)]), np.uint64)
         self.n = len(self.slots_np)
         self.slots = torch.from_numpy(self.slots_np.view(np.int64)).cuda()
+        step_bytes = self.n * self.heads * self.hd * 2 * 2 * 2 + self.n * 8
+        # Timed write launches rotate over `rot` slot sets (the step's slots,
+        # then each sequence's `new` positions before them, ...) with their own
+        # input rows, so that one rotation touches more than the 126 MB L2.
+        self.rot = int(min(pre // new, max(2, -(-2 * 126_000_000 // step_bytes))))
+        self.rot_slots = [self.slots] + [
+            torch.from_numpy(np.array(kv.build_slot_mapping([(s, p) for s in b.sequences
+                                                             for p in range(pre - new * r, pre - new * r + new)]),
+                                      np.uint64).view(np.int64)).cuda() for r in range(1, self.rot)]
         gen = torch.Generator(device="cuda")
         gen.manual_seed(cfg["seed"] + 17 * rank)
-        self.k_new = torch.randn(self.n * self.heads * self.hd, generator=gen, device="cuda").to(torch.bfloat16)
-        self.v_new = torch.randn_like(self.k_new, dtype=torch.float32).to(torch.bfloat16)
+        rows = self.n * self.heads * self.hd
+        self.k_rot = torch.randn(self.rot * rows, generator=gen, device="cuda").to(torch.bfloat16)
+        self.v_rot = torch.randn_like(self.k_rot, dtype=torch.float32).to(torch.bfloat16)
+        self.k_new, self.v_new = self.k_rot[:rows], self.v_rot[:rows]
+        self.turn = 0
         table, self.width = b.table()
         self.table = torch.from_numpy(table.view(np.int64)).cuda()
         self.lens = torch.full((nseq,), self.total_len, dtype=torch.int64, device="cuda")
@@ -498,8 +510,12 @@ class WriteGather:
         self.gather_bytes = 2 * 2 * nseq * per * 2 + table.nbytes  # read+write K,V + table
 
     def write(self, stream):
-        self.kv.check(self.kv.lib.kvfx_write(ctypes.byref(self.desc), self.k_new.data_ptr(), self.v_new.data_ptr(),
-                                             self.slots.data_ptr(), self.n, stream), "kvfx_write")
+        r = self.turn % self.rot
+        self.turn += 1
+        off = r * self.n * self.heads * self.hd * 2
+        self.kv.check(self.kv.lib.kvfx_write(ctypes.byref(self.desc), self.k_rot.data_ptr() + off,
+                                             self.v_rot.data_ptr() + off, self.rot_slots[r].data_ptr(), self.n,
+                                             stream), "kvfx_write")
 
     def gather(self, stream):
         self.kv.check(self.kv.lib.kvfx_gather_batch(ctypes.byref(self.desc), self.table.data_ptr(),
@@ -590,7 +606,10 @@ def layer_batches(kv, w, rank: int, world: int, ranks: Ranks, layers: int = 32, 
     one kvfx_write_layers launch. Gather: every sequence's K/V of every layer
     to contiguous per-layer runs in one kvfx_gather_layers launch. The caches
     hold whatever the allocation held: the timing does not depend on the
-    values (the tests check the bytes)."""
+    values (the tests check the bytes). Successive write launches rotate over
+    `rot` slot sets (each sequence's last 4 positions, the 4 before them, ...)
+    and as many input buffers, so that one rotation touches more bytes than
+    the 126 MB L2 holds and every launch reads and writes HBM."""
     import torch
 
     heads, hd, bs = 8 // world, 128, 16
@@ -599,15 +618,18 @@ def layer_batches(kv, w, rank: int, world: int, ranks: Ranks, layers: int = 32, 
     dev = torch.cuda.current_device()
     stores = [kv.PagedKVStorage(b.pool, heads, hd, kv.DType.BFloat16, dev) for _ in range(layers)]
     arr = (kv.KvfxCache * layers)(*[kv.cache_descriptor(st) for st in stores])
-    slots = np.array(kv.build_slot_mapping([(s, p) for s in b.sequences for p in range(total - new, total)]),
-                     np.uint64)
-    n = len(slots)
-    slots_d = torch.from_numpy(slots.view(np.int64)).cuda()
     row = heads * hd * 2
+    rot = max(2, -(-2 * 126_000_000 // max(1, layers * nseq * new * row * 2 * 2)))
+    slot_sets = [np.array(kv.build_slot_mapping([(s, p) for s in b.sequences
+                                                 for p in range(total - new * (r + 1), total - new * r)]), np.uint64)
+                 for r in range(rot)]
+    n = len(slot_sets[0])
+    slots_d = [torch.from_numpy(sl.view(np.int64)).cuda() for sl in slot_sets]
     gen = torch.Generator(device="cuda")
     gen.manual_seed(0xC0F2 * 3 + rank)
-    k_new = torch.randn(layers * n * heads * hd, generator=gen, device="cuda").to(torch.bfloat16)
+    k_new = torch.randn(rot * layers * n * heads * hd, generator=gen, device="cuda").to(torch.bfloat16)
     v_new = torch.randn_like(k_new, dtype=torch.float32).to(torch.bfloat16)
+    in_bytes = layers * n * row  # one launch's K (or V) input
     table, width = b.table()
     table_d = torch.from_numpy(table.view(np.int64)).cuda()
     lens_d = torch.full((nseq,), total, dtype=torch.int64, device="cuda")
@@ -619,9 +641,13 @@ def layer_batches(kv, w, rank: int, world: int, ranks: Ranks, layers: int = 32, 
     vp = torch.tensor([v_out.data_ptr() + i * layers * per_layer for i in range(nseq)], dtype=torch.int64,
                       device="cuda")
 
+    turn = [0]
+
     def write(stream):
-        kv.check(kv.lib.kvfx_write_layers(arr, layers, k_new.data_ptr(), v_new.data_ptr(), n * row,
-                                          slots_d.data_ptr(), n, stream), "kvfx_write_layers")
+        r = turn[0] % rot
+        turn[0] += 1
+        kv.check(kv.lib.kvfx_write_layers(arr, layers, k_new.data_ptr() + r * in_bytes, v_new.data_ptr() + r * in_bytes,
+                                          n * row, slots_d[r].data_ptr(), n, stream), "kvfx_write_layers")
 
     def gather(stream):
         kv.check(kv.lib.kvfx_gather_layers(arr, layers, table_d.data_ptr(), lens_d.data_ptr(), nseq, width,
@@ -640,7 +666,9 @@ def layer_batches(kv, w, rank: int, world: int, ranks: Ranks, layers: int = 32, 
     g_bytes = ranks.reduce(float(layers * nseq * total * row * 2 * 2 + table.nbytes), "sum")
     out = {"workload": f"{layers} layers x config2 shapes (8 KV heads x 128 bf16), one storage per layer on one "
                        f"8192-page odd/even pool, 64 sequences x 1024 tokens",
-           "write_tokens": n, "write_ms_per_launch": w_ms, "write_layer_tokens_per_s": layers * n / (w_ms * 1e-3),
+           "write_tokens": n, "write_rotation": f"{rot} slot/input sets, {rot * w_bytes / world / 1e6:.0f} MB "
+                                                 f"touched per rotation (L2 126 MB)",
+           "write_ms_per_launch": w_ms, "write_layer_tokens_per_s": layers * n / (w_ms * 1e-3),
            "write_gbs": w_bytes / (w_ms * 1e-3) / 1e9,
            "write_frac_of_peak": w_bytes / (w_ms * 1e-3) / 1e9 / (peak * world),
            "write_graph_ms_per_launch": wg_ms if graph else None,
@@ -1063,7 +1091,9 @@ def main(argv=None) -> int:
             "graph_tokens_per_s": wg.n / (g_ms_launch * 1e-3), "graph_ms_per_launch": g_ms_launch,
             "graph_hbm_gbs": write_bytes_all / (g_ms_launch * 1e-3) / 1e9,
             "graph_frac_of_peak": write_bytes_all / (g_ms_launch * 1e-3) / 1e9 / (peak * world),
-            "e2e_tokens_per_s": wg.n / (e2e_w_ms * 1e-3), "e2e_h2d_bytes_per_step": e2e_w_h2d * world}
+            "e2e_tokens_per_s": wg.n / (e2e_w_ms * 1e-3), "e2e_h2d_bytes_per_step": e2e_w_h2d * world,
+            "l2": f"timed launches rotate over {wg.rot} slot/input sets "
+                  f"({wg.rot * wg.write_bytes / 1e6:.0f} MB touched per rotation, L2 126 MB)"}
         secondary["gather"] = {
             "workload": "config2 gather: 64 seqs x 8192 tokens to contiguous K/V, one kvfx_gather_batch launch",
             "gbs": gather_bytes_all / (g_ms * 1e-3) / 1e9, "ms_per_step": g_ms,
