@@ -92,13 +92,15 @@ private:
     static constexpr std::size_t kNone = std::numeric_limits<std::size_t>::max();
     enum class State : std::uint8_t { Free, Active, Idle };
     // What every handle check reads, packed densely: validating a large page
-    // table touches only this array.
+    // table touches only this array. 16 bytes, so that no slot straddles two
+    // cache lines (one miss per checked entry).
     struct Slot {
         std::uint64_t generation = 0;
-        std::size_t refs = 0;
+        std::uint32_t refs = 0;
         State state = State::Free;
         bool published = false;
     };
+    static_assert(sizeof(Slot) == 16, "Slot must pack into 16 bytes");
     // What only publish/lookup/eviction read.
     struct SlotMeta {
         std::uint64_t hash = 0;

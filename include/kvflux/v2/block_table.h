@@ -36,7 +36,7 @@ public:
     }
     // out[j] = physical_id(j) for every entry (the same checks and
     // exceptions, in entry order), with the pool's bookkeeping of entry
-    // j + 16 prefetched while entry j is checked: entries are random pages,
+    // j + 32 prefetched while entry j is checked: entries are random pages,
     // so one lookup after another would wait on a cache miss each.
     void copy_ids(PhysicalBlockID* out) const;
     std::size_t size() const noexcept { return entries_.size(); }
@@ -64,7 +64,7 @@ inline PhysicalBlockID BlockTable::physical_id(std::size_t logical_block) const 
 }
 
 inline void BlockTable::copy_ids(PhysicalBlockID* out) const {
-    constexpr std::size_t kAhead = 16;
+    constexpr std::size_t kAhead = 32;
     const std::size_t n = entries_.size();
     for (std::size_t j = 0; j < n && j < kAhead; ++j) pool_->prefetch(entries_[j]);
     for (std::size_t j = 0; j < n; ++j) {

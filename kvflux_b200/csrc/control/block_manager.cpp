@@ -78,7 +78,7 @@ BlockHandle BlockManager::allocate() {
 
 void BlockManager::retain(BlockHandle h) {
     Slot& s = live(h);
-    if (s.refs == std::numeric_limits<std::size_t>::max()) {
+    if (s.refs == std::numeric_limits<std::uint32_t>::max()) {
         throw std::overflow_error("block reference count exhausted");
     }
     if (s.state == State::Idle) {
