@@ -39,6 +39,10 @@ __global__ void __launch_bounds__(256) write_kernel(
         const Idx c = i - row * vpr;
         const Idx tok = row / heads;
         const Idx h = row - tok * heads;
+        // The row's data and its slot are loaded together (neither depends
+        // on the other), so the thread waits for one memory latency, not two.
+        const auto kv = __ldg(k_new + i);
+        const auto vv = __ldg(v_new + i);
         const uint64_t slot = __ldg(slots + tok);
         if (slot >= slot_count) {
             raise_flag(status, KVFX_FLAG_BAD_INDEX);
@@ -47,8 +51,6 @@ __global__ void __launch_bounds__(256) write_kernel(
         const uint64_t page = slot / bs;
         const uint64_t off = slot - page * bs;
         const uint64_t dst = ((page * heads + h) * bs + off) * vpr + c;
-        const auto kv = __ldg(k_new + i);
-        const auto vv = __ldg(v_new + i);
         k_cache[dst] = kv;
         v_cache[dst] = vv;
     }
@@ -312,6 +314,19 @@ __global__ void __launch_bounds__(256) write_layers_kernel(
     for (uint32_t base = blockIdx.x * blockDim.x * kWriteLayersPer; base < total; base += span) {
         uint4 kx[kWriteLayersPer], vx[kWriteLayersPer];
         uint64_t dst[kWriteLayersPer];
+        // Data and slots are loaded before any slot is examined: the data
+        // loads do not depend on the slots, so both latencies overlap.
+        uint64_t slot[kWriteLayersPer];
+#pragma unroll
+        for (int j = 0; j < kWriteLayersPer; ++j) {
+            const uint32_t i = base + j * blockDim.x + threadIdx.x;
+            slot[j] = ~0ull;
+            if (i < total) {
+                kx[j] = __ldg(kn + i);
+                vx[j] = __ldg(vn + i);
+                slot[j] = __ldg(slots + i / vpr / heads);
+            }
+        }
 #pragma unroll
         for (int j = 0; j < kWriteLayersPer; ++j) {
             const uint32_t i = base + j * blockDim.x + threadIdx.x;
@@ -321,13 +336,10 @@ __global__ void __launch_bounds__(256) write_layers_kernel(
                 const uint32_t c = i - row * vpr;
                 const uint32_t tok = row / heads;
                 const uint32_t h = row - tok * heads;
-                const uint64_t slot = __ldg(slots + tok);
-                if (slot < slot_count) {
-                    const uint64_t page = slot / bs;
-                    const uint64_t off = slot - page * bs;
+                if (slot[j] < slot_count) {
+                    const uint64_t page = slot[j] / bs;
+                    const uint64_t off = slot[j] - page * bs;
                     dst[j] = ((page * heads + h) * bs + off) * vpr + c;
-                    kx[j] = __ldg(kn + i);
-                    vx[j] = __ldg(vn + i);
                 } else {
                     raise_flag(status, KVFX_FLAG_BAD_INDEX);
                 }
