@@ -40,4 +40,24 @@ void paged_attention_batch_host(const PagedKVStorage& storage,
                                 const float* query_host, float* output_host,
                                 std::size_t query_heads);
 
+// paged_attention over several sequences of one storage in one call (a
+// prefill batch); no counterpart in the reference, whose callers make one
+// paged_attention call per sequence. Sequence i has query_tokens[i] queries
+// in queries_device[i] and its output in outputs_device[i] (each
+// [query_tokens[i]][query_heads][head_size] FP32 on the storage's device).
+// paged_attention's checks run over the batch in two passes, each in
+// sequence order: pool, shape, size overflow, null pointers and page ids of
+// every sequence, then the device and overlap checks of every sequence; last,
+// no output may overlap another sequence's Q or O (invalid_argument). The
+// arrays must all have sequences.size() entries. Sequences with no queries
+// are skipped. Outputs are bit-identical to one paged_attention per sequence; the
+// tensor-core shapes of up to KVFX_MAX_PREFILL_SEQS sequences at a time share
+// one persistent launch. Synchronous on the legacy default stream.
+void paged_attention_prefill_batch(const PagedKVStorage& storage,
+                                   const std::vector<const SequenceState*>& sequences,
+                                   const std::vector<const float*>& queries_device,
+                                   const std::vector<float*>& outputs_device,
+                                   const std::vector<std::size_t>& query_tokens,
+                                   std::size_t query_heads);
+
 } // namespace kvflux::v2

@@ -59,6 +59,107 @@ void paged_attention(const PagedKVStorage& storage, const SequenceState& sequenc
     rt.finish("paged attention synchronize");
 }
 
+void paged_attention_prefill_batch(const PagedKVStorage& storage, const std::vector<const SequenceState*>& sequences,
+                                   const std::vector<const float*>& queries_device,
+                                   const std::vector<float*>& outputs_device,
+                                   const std::vector<std::size_t>& query_tokens, std::size_t query_heads) {
+    const std::size_t n = sequences.size();
+    if (queries_device.size() != n || outputs_device.size() != n || query_tokens.size() != n) {
+        throw std::invalid_argument("prefill batch arrays differ in length");
+    }
+    const PagedKVLayout& layout = storage.layout();
+    // Per sequence, paged_attention's checks in its order.
+    std::vector<std::size_t> live;       // sequences with queries
+    std::vector<std::size_t> io_bytes(n, 0);
+    std::vector<ReadBlockTable> tables(n);
+    std::size_t widest = 0;
+    for (std::size_t i = 0; i < n; ++i) {
+        const SequenceState* seq = sequences[i];
+        if (seq == nullptr) throw std::invalid_argument("null sequence in prefill batch");
+        if (!storage.uses_pool(seq->block_table())) {
+            throw std::invalid_argument("sequence and KV storage must use one physical pool");
+        }
+        if (seq->block_size() != layout.block_size() || query_heads == 0 ||
+            query_heads % layout.num_kv_heads() != 0 || query_tokens[i] > seq->num_tokens()) {
+            throw std::invalid_argument("invalid paged attention shape");
+        }
+        const std::size_t elements = detail::mul_checked(
+            detail::mul_checked(query_tokens[i], query_heads, "paged attention"), layout.head_size(),
+            "paged attention");
+        io_bytes[i] = detail::mul_checked(elements, sizeof(float), "paged attention");
+        if (query_tokens[i] == 0) continue;
+        if (queries_device[i] == nullptr || outputs_device[i] == nullptr) {
+            throw std::invalid_argument("Q and attention output device pointers are required");
+        }
+        tables[i] = build_read_block_table(*seq);
+        for (const PhysicalBlockID b : tables[i]) {
+            if (b >= layout.num_blocks()) throw std::out_of_range("attention block out of range");
+        }
+        widest = std::max(widest, tables[i].size());
+        live.push_back(i);
+    }
+    if (live.empty()) return;
+    detail::DeviceGuard guard(storage.device());
+    for (const std::size_t i : live) {
+        detail::require_device_pointer(queries_device[i], storage.device(), "Q");
+        detail::require_device_pointer(outputs_device[i], storage.device(), "attention output");
+        if (detail::overlaps(queries_device[i], io_bytes[i], outputs_device[i], io_bytes[i]) ||
+            detail::overlaps(queries_device[i], io_bytes[i], storage.key_base(), layout.total_bytes()) ||
+            detail::overlaps(outputs_device[i], io_bytes[i], storage.key_base(), layout.total_bytes())) {
+            throw std::invalid_argument("Q and attention output must not overlap each other or KV cache");
+        }
+    }
+    // One launch runs the sequences concurrently: an output must not overlap
+    // another sequence's Q or O (one call after another would define it).
+    for (const std::size_t i : live) {
+        for (const std::size_t j : live) {
+            if (i == j) continue;
+            if (detail::overlaps(outputs_device[i], io_bytes[i], outputs_device[j], io_bytes[j]) ||
+                detail::overlaps(outputs_device[i], io_bytes[i], queries_device[j], io_bytes[j])) {
+                throw std::invalid_argument("prefill batch outputs must not overlap other sequences' Q or O");
+            }
+        }
+    }
+    const std::size_t rows = live.size();
+    const std::size_t table_bytes = detail::mul_checked(detail::mul_checked(rows, widest, "paged attention"),
+                                                        sizeof(PhysicalBlockID), "paged attention");
+    std::vector<PhysicalBlockID> table(rows * widest, BatchBlockTable::invalid_block());
+    for (std::size_t r = 0; r < rows; ++r) {
+        const ReadBlockTable& t = tables[live[r]];
+        std::copy(t.begin(), t.end(), table.begin() + r * widest);
+    }
+    detail::StorageRuntime& rt = storage.runtime();
+    const void* host[1] = {table.data()};
+    void* dev[1] = {nullptr};
+    rt.upload(host, &table_bytes, 1, dev);
+    const uint32_t qh = static_cast<uint32_t>(query_heads);
+    std::size_t ws_bytes = 0;
+    for (const std::size_t i : live) {
+        ws_bytes = std::max<std::size_t>(
+            ws_bytes, kvfx_attention_workspace_bytes(&rt.cache, query_tokens[i], sequences[i]->num_tokens(), qh));
+    }
+    void* ws = rt.ensure_workspace(ws_bytes);
+    const auto* table_dev = static_cast<const uint64_t*>(dev[0]);
+    for (std::size_t r0 = 0; r0 < rows; r0 += KVFX_MAX_PREFILL_SEQS) {
+        const std::size_t r1 = std::min<std::size_t>(rows, r0 + KVFX_MAX_PREFILL_SEQS);
+        const float* q[KVFX_MAX_PREFILL_SEQS];
+        float* o[KVFX_MAX_PREFILL_SEQS];
+        uint64_t qt[KVFX_MAX_PREFILL_SEQS], kt[KVFX_MAX_PREFILL_SEQS];
+        for (std::size_t r = r0; r < r1; ++r) {
+            const std::size_t i = live[r];
+            q[r - r0] = queries_device[i];
+            o[r - r0] = outputs_device[i];
+            qt[r - r0] = query_tokens[i];
+            kt[r - r0] = sequences[i]->num_tokens();
+        }
+        detail::check_kvfx(kvfx_attention_batch(&rt.cache, static_cast<uint32_t>(r1 - r0), q, o,
+                                                table_dev + r0 * widest, widest, qt, kt, qh, ws,
+                                                rt.workspace_bytes, nullptr),
+                           "paged attention prefill batch");
+    }
+    rt.finish("paged attention prefill batch synchronize");
+}
+
 namespace {
 
 // Device address of page-locked host memory (cudaHostAlloc / cudaHostRegister),

@@ -231,6 +231,15 @@ PYBIND11_MODULE(_C, m) {
                                            py::object q, py::object o, std::size_t query_heads) {
         paged_attention_batch_host(s, seqs, ptr<const float>(q), ptr<float>(o), query_heads);
     });
+    m.def("paged_attention_prefill_batch",
+          [](const PagedKVStorage& s, const std::vector<const SequenceState*>& seqs, const py::list& qs,
+             const py::list& os, const std::vector<std::size_t>& query_tokens, std::size_t query_heads) {
+              std::vector<const float*> q;
+              std::vector<float*> o;
+              for (const auto& x : qs) q.push_back(ptr<const float>(py::reinterpret_borrow<py::object>(x)));
+              for (const auto& x : os) o.push_back(ptr<float>(py::reinterpret_borrow<py::object>(x)));
+              paged_attention_prefill_batch(s, seqs, q, o, query_tokens, query_heads);
+          });
     m.def("append_token_cow", &append_token_cow);
     m.def("write_paged_kv_layers", [](const std::vector<PagedKVStorage*>& layers, py::object k, py::object v,
                                       const SlotMapping& slots) {

@@ -6,7 +6,10 @@ single-sequence path), and within max_abs_err 2e-3 (BF16/FP16) / 1e-5 (FP32)
 of the FP64 oracle on the last rows of each sequence. Ragged batches mix
 lengths whose query tiles run out at different unit rounds, single-query
 sequences (batch-decode kernel), empty ones (skipped) and FP32 caches
-(generic kernel)."""
+(generic kernel). The C++ API over it, paged_attention_prefill_batch, is
+bit-identical to one paged_attention per sequence (also past one launch's
+KVFX_MAX_PREFILL_SEQS sequences) and raises the reference's exception types
+for bad shapes, foreign pools and overlapping buffers."""
 import ctypes
 
 import numpy as np
@@ -122,5 +125,82 @@ def test_batch_argument_errors():
     assert f(d, 2, qq, oo, td.data_ptr(), 3, _u64s([4, 1]), _u64s([40, 20]), qh, None, 0, None) == kv.KVFX_ENOSPACE
     assert f(d, 0, None, None, None, 0, None, None, qh, None, 0, None) == kv.KVFX_OK            # nothing to do
     assert f(d, 2, qq, oo, None, 0, _u64s([0, 0]), _u64s([40, 20]), qh, None, 0, None) == kv.KVFX_OK
+    torch.cuda.synchronize()
+    assert kv.device_status(0) == 0
+
+
+# -------------------------------------------------------------- C++ API ---
+
+def _storage_case(dtype, kvh, hd, lens, seed):
+    bs = 16
+    batch = w.decode_batch_on_pool(sum((l + bs - 1) // bs for l in lens) + 8, bs, lens, seed=seed)
+    st = kv.PagedKVStorage(batch.pool, kvh, hd, w.DTYPES[dtype], 0)
+    total = sum(lens)
+    view = np.int16 if dtype != "float32" else np.float32
+    k = w.encode(w.normal(seed + 1, total * kvh * hd), dtype).view(view)
+    v = w.encode(w.normal(seed + 2, total * kvh * hd), dtype).view(view)
+    writes = [(s, t) for s in batch.sequences for t in range(s.num_tokens())]
+    kv.write_paged_kv(st, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), kv.build_slot_mapping(writes))
+    return batch, st
+
+
+@pytest.mark.parametrize("dtype,kvh,group,hd,lens,lq", [
+    ("bfloat16", 2, 4, 128, [300, 77, 129, 40], [300, 0, 64, 1]),
+    ("float32", 2, 2, 64, [50, 33], [50, 7]),
+])
+def test_api_prefill_batch_bit_identical_to_paged_attention(dtype, kvh, group, hd, lens, lq):
+    batch, st = _storage_case(dtype, kvh, hd, lens, seed=sum(lens))
+    qh = kvh * group
+    qs = [torch.from_numpy(w.normal(60 + i, max(a, 1) * qh * hd)).cuda() for i, a in enumerate(lq)]
+    outs = [torch.full((max(a, 1) * qh * hd,), 3.0, device="cuda") for a in lq]
+    kv.paged_attention_prefill_batch(st, batch.sequences, qs, outs, lq, qh)
+    for i, a in enumerate(lq):
+        if a == 0:
+            assert (outs[i].cpu().numpy() == 3.0).all(), "sequence without queries written"
+            continue
+        one = torch.empty_like(outs[i])
+        kv.paged_attention(st, batch.sequences[i], qs[i], one, a, qh)
+        assert torch.equal(outs[i].view(torch.int32), one.view(torch.int32)), f"sequence {i}"
+    assert kv.device_status(0) == 0
+
+
+def test_api_prefill_batch_more_sequences_than_one_launch():
+    n = kv.KVFX_MAX_PREFILL_SEQS + 8
+    lens = [int(x) for x in w.uniform_ints(17, n, 2, 200)]
+    batch, st = _storage_case("float16", 1, 128, lens, seed=77)
+    qh = 4
+    qs = [torch.from_numpy(w.normal(500 + i, L * qh * 128)).cuda() for i, L in enumerate(lens)]
+    outs = [torch.empty(L * qh * 128, device="cuda") for L in lens]
+    kv.paged_attention_prefill_batch(st, batch.sequences, qs, outs, lens, qh)
+    for i, L in enumerate(lens):
+        one = torch.empty_like(outs[i])
+        kv.paged_attention(st, batch.sequences[i], qs[i], one, L, qh)
+        assert torch.equal(outs[i].view(torch.int32), one.view(torch.int32)), f"sequence {i}"
+
+
+def test_api_prefill_batch_errors():
+    batch, st = _storage_case("bfloat16", 2, 128, [40, 30], seed=3)
+    other = kv.PhysicalBlockPool(8, 16)
+    foreign = kv.SequenceState(9, other)
+    foreign.append_tokens(5)
+    qh = 8
+    q = torch.zeros(40 * qh * 128, device="cuda")
+    o = torch.zeros_like(q)
+    o2 = torch.zeros_like(q)
+    seqs = batch.sequences
+    with pytest.raises(ValueError):   # array lengths differ
+        kv.paged_attention_prefill_batch(st, seqs, [q], [o, o2], [4, 4], qh)
+    with pytest.raises(ValueError):   # more queries than tokens
+        kv.paged_attention_prefill_batch(st, seqs, [q, q], [o, o2], [41, 4], qh)
+    with pytest.raises(ValueError):   # sequence of another pool
+        kv.paged_attention_prefill_batch(st, [seqs[0], foreign], [q, q], [o, o2], [4, 4], qh)
+    with pytest.raises(ValueError):   # two outputs overlap
+        kv.paged_attention_prefill_batch(st, seqs, [q, q], [o, o], [4, 4], qh)
+    with pytest.raises(ValueError):   # an output overlaps another sequence's Q
+        kv.paged_attention_prefill_batch(st, seqs, [q, o2], [o2, o], [4, 4], qh)
+    with pytest.raises(ValueError):   # head count not a multiple of the KV heads
+        kv.paged_attention_prefill_batch(st, seqs, [q, q], [o, o2], [4, 4], 3)
+    kv.paged_attention_prefill_batch(st, seqs, [None, None], [None, None], [0, 0], qh)  # nothing to do
+    kv.paged_attention_prefill_batch(st, [], [], [], [], qh)
     torch.cuda.synchronize()
     assert kv.device_status(0) == 0
