@@ -2,9 +2,16 @@
 // host work (the padded batch page table of paged_attention_batch): the
 // caller and up to kMaxWorkers threads take chunks of rows from a shared
 // counter. One job runs at a time; concurrent callers queue on a mutex.
+// The pool is sized to the CPUs this process may run on, shared among the
+// processes of one node when a launcher says how many there are
+// (LOCAL_WORLD_SIZE, one process per GPU): a worker preempted while it holds
+// a chunk would hold up the whole job.
+#include <sched.h>
+
 #include <algorithm>
 #include <atomic>
 #include <condition_variable>
+#include <cstdlib>
 #include <exception>
 #include <mutex>
 #include <thread>
@@ -16,11 +23,27 @@ namespace {
 
 constexpr unsigned kMaxWorkers = 7;
 
+// CPUs in this process's affinity mask (all CPUs if it cannot be read),
+// divided among LOCAL_WORLD_SIZE processes when that is set above 1.
+unsigned usable_cpus() {
+    unsigned cpus = std::thread::hardware_concurrency();
+    cpu_set_t set;
+    CPU_ZERO(&set);
+    if (sched_getaffinity(0, sizeof(set), &set) == 0 && CPU_COUNT(&set) > 0) {
+        cpus = static_cast<unsigned>(CPU_COUNT(&set));
+    }
+    if (const char* s = std::getenv("LOCAL_WORLD_SIZE")) {
+        const long procs = std::strtol(s, nullptr, 10);
+        if (procs > 1) cpus = std::max(1u, cpus / static_cast<unsigned>(procs));
+    }
+    return cpus;
+}
+
 class Pool {
 public:
     Pool() {
-        const unsigned hw = std::thread::hardware_concurrency();
-        const unsigned n = hw > 1 ? std::min(kMaxWorkers, hw - 1) : 0;
+        const unsigned cpus = usable_cpus();
+        const unsigned n = cpus > 1 ? std::min(kMaxWorkers, cpus - 1) : 0;
         for (unsigned i = 0; i < n; ++i) workers_.emplace_back([this] { loop(); });
     }
 
