@@ -9,19 +9,24 @@ timed region has no collective. `value` = KV bytes of all ranks / max-over-
 ranks time per step (strong scaling: the job is fixed, N splits it).
 
 The same JSON line carries: `e2e` (the same metric through the drop-in C++
-API paged_attention_batch with Q on pinned host memory, H2D + D2H inside the
-timed region), `roofline` of the decode kernel, `cpu_baseline` (the
-reference's CPU path on a bounded sample, rank 0 at N=1), clocks, and
-`secondary` lines: KV-write tokens/s and gather GB/s on config 2 (64
-sequences x 8192 tokens, 256 new tokens per step, odd/even fragmented
-65,536-page pool) and decode GB/s on config 3 (Llama-3-8B heads, batch 64,
-lengths in [512, 8192]).
+API, paged_attention_batch_host with Q and O in pinned host memory, H2D + D2H
+inside the timed region), `roofline` of the decode kernel, `cpu_baseline`
+(the reference's CPU path on a bounded sample, rank 0 at N=1, with the
+reference's own GPU kernels timed beside this build's), clocks, and
+`secondary` lines: config 5 as a serving decode step (append + fused write
+and decode through BatchDecodeSession), KV-write tokens/s and gather GB/s on
+config 2 (64 sequences x 8192 tokens, 256 new tokens per step, odd/even
+fragmented 65,536-page pool), decode GB/s on config 3 (Llama-3-8B heads,
+batch 64, lengths in [512, 8192]), config 2's shapes over 32 layers (layer-
+batched write and gather) and config 4's prefix-sharing prefill (8 x 4096
+tokens in one batched tcgen05 launch; rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-Inputs are synthetic (seeded). Decode and gather inputs are far larger than
-the 126 MB L2, so no flush is needed between timed steps; the 2 MB write
-step is reported per launch and over graph-captured back-to-back launches.
+Inputs are synthetic (seeded). Decode, gather and prefill inputs are far
+larger than the 126 MB L2, so no flush is needed between timed steps; the
+write launches rotate over slot/input sets that together exceed L2, and are
+reported per launch and over graph-captured back-to-back launches.
 """
 from __future__ import annotations
 
