@@ -338,9 +338,12 @@ void batch_decode(const PagedKVStorage& storage, const std::vector<const Sequenc
     // ~0.3 ms of upload while the kernel saturates HBM), and the two kernels
     // take as long as one launch over every row.
     // With host I/O the first chunk also waits for its Q upload (measured at
-    // config 5 per call: a quarter of the rows first 2.82-2.92 ms, a third
+    // config 5 per call: a quarter of the rows first 2.80-2.92 ms, a third
     // 2.85, a half 3.08, an eighth 2.96; with the second chunk's Q issued
-    // before the first chunk's table, 2.85).
+    // before the first chunk's table, 2.85; three chunks - a sixteenth on the
+    // default stream, the rest of the first quarter on the side stream, the
+    // last three quarters on the default stream after the first kernel -
+    // 2.89).
     const std::size_t head_rows = batch >= 16 ? (batch + 3) / 4 : batch;
     const std::size_t ws0 = workspace_of(0, head_rows);
     const std::size_t ws1 = head_rows < batch ? workspace_of(head_rows, batch) : 0;
