@@ -876,8 +876,15 @@ def reference_arm(args, ranks: Ranks) -> int:
     shapes; each step is a bounded sample of requests (one per thread)."""
     if ranks.rank != 0:
         return 0
+    import importlib.util
+
     import oracle
-    from kvflux_b200 import workloads as w
+
+    # The seeded generators by file path: importing the kvflux_b200 package
+    # would load this build's native library into the reference's process.
+    spec = importlib.util.spec_from_file_location("kvflux_synth", ROOT / "kvflux_b200" / "synth.py")
+    w = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(w)
 
     cfg = w.CONFIG5
     threads = cpu_threads()

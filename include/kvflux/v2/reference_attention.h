@@ -5,8 +5,8 @@
 // [query_tokens][query_heads][head_size], K/V [kv_tokens][kv_heads][head_size];
 // Q is the suffix of the K/V sequence.
 //
-// This function is implemented by the oracle library (oracle/), which is test
-// infrastructure; the GPU data plane never calls it.
+// A host function of libkvflux_b200 (as in KVFlux's library), for programs
+// that check the GPU kernels against it; no GPU entry point calls it.
 #include <cstddef>
 #include <vector>
 

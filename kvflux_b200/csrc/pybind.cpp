@@ -17,6 +17,7 @@
 #include "kvflux/v2/paged_kv_storage.h"
 #include "kvflux/v2/paged_kv_write.h"
 #include "kvflux/v2/prefix_cache.h"
+#include "kvflux/v2/reference_attention.h"
 #include "kvflux/v2/sequence_lifecycle.h"
 #include "kvflux/v2/slot_mapping.h"
 
@@ -174,6 +175,16 @@ PYBIND11_MODULE(_C, m) {
         return build_slot_mapping(to_writes(batch));
     });
     m.def("build_read_block_table", &build_read_block_table);
+    m.def(
+        "reference_attention",
+        [](const std::vector<float>& q, const std::vector<float>& k, const std::vector<float>& v,
+           std::size_t query_tokens, std::size_t kv_tokens, std::size_t query_heads, std::size_t kv_heads,
+           std::size_t head_size) {
+            return reference_attention(q, k, v, AttentionShape{query_tokens, kv_tokens, query_heads, kv_heads,
+                                                               head_size});
+        },
+        py::arg("query"), py::arg("key"), py::arg("value"), py::arg("query_tokens"), py::arg("kv_tokens"),
+        py::arg("query_heads"), py::arg("kv_heads"), py::arg("head_size"));
 
     py::class_<PagedKVLayout>(m, "PagedKVLayout")
         .def(py::init<std::size_t, std::size_t, std::size_t, std::size_t, DType>())

@@ -3,9 +3,10 @@
   oracle/libkvoracle.so        - kvoracle.c, the CPU restatement of the path
   oracle/_ref/libkvflux_ref.so - the reference's own CPU sources (control plane
                                  and reference_attention) + ref_shim.cpp, built
-                                 from the reference checkout when one is present
-                                 (KVFLUX_REFERENCE, default: the checkout mounted
-                                 next to this repository in the build container).
+                                 from a KVFlux checkout when one is found
+                                 (--reference PATH, else $KVFLUX_REFERENCE, else a
+                                 directory named "reference" beside this
+                                 repository's own directory).
                                  The built file travels with the tree; the
                                  sources are never copied into it.
   oracle/_ref/libkvflux_ref_gpu.so - the reference's own GPU path (its CPU
@@ -14,7 +15,7 @@
                                  with nvcc for sm_100a + ref_gpu_shim.cpp: the
                                  GPU-side baseline and an independent parity check.
 
-Usage: python oracle/build.py [--force]
+Usage: python oracle/build.py [--force] [--reference PATH]
 """
 from __future__ import annotations
 
@@ -54,8 +55,20 @@ REF_SOURCES = [
 ]
 
 
+_REFERENCE_OVERRIDE: Path | None = None
+
+
 def reference_root() -> Path:
-    return Path(os.environ.get("KVFLUX_REFERENCE", "/root/reference"))
+    """The KVFlux checkout whose sources the reference builds use: the
+    --reference argument, else $KVFLUX_REFERENCE, else a sibling directory
+    named "reference" next to this repository. It need not exist: without it
+    only the C restatement is built."""
+    if _REFERENCE_OVERRIDE is not None:
+        return _REFERENCE_OVERRIDE
+    env = os.environ.get("KVFLUX_REFERENCE")
+    if env:
+        return Path(env)
+    return HERE.parent.parent / "reference"
 
 
 def _run(cmd: list[str]) -> None:
@@ -100,7 +113,11 @@ def build(force: bool = False) -> dict:
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--force", action="store_true")
+    ap.add_argument("--reference", type=Path, default=None, help="KVFlux checkout to build the reference from")
     args = ap.parse_args(argv)
+    global _REFERENCE_OVERRIDE
+    if args.reference is not None:
+        _REFERENCE_OVERRIDE = args.reference.resolve()
     for k, v in build(force=args.force).items():
         print(f"{k}: {v}")
     return 0
