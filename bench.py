@@ -317,16 +317,16 @@ def time_launches(launch, steps: int, warmup: int, ranks: Ranks):
 def e2e_decode(kv, wl: Decode, steps: int, warmup: int):
     """Same metric end to end from host buffers. Headline: one
     paged_attention_batch_host call per step (Q from pinned host memory,
-    uploaded per row chunk ahead of that chunk's kernel; block table and
-    lengths built and uploaded by the call; O written into pinned host memory
-    by the kernels; synchronous). Beside it: the device-buffer API with an
+    uploaded per row chunk ahead of that chunk's kernel; the lengths uploaded
+    and the device-resident page table refreshed by the call - unchanged rows
+    re-send nothing; O written into pinned host memory by the kernels;
+    synchronous). Beside it: the device-buffer API with an
     explicit Q copy before and O copy after (the reference's call shape)."""
     import torch
 
     q_host = wl.q.cpu().pin_memory()
     o_host = torch.empty_like(q_host).pin_memory()
     seqs = wl.b.sequences
-    table_bytes = wl.batch * wl.width * 8 + wl.batch * 8
 
     def step_host():
         kv.paged_attention_batch_host(wl.storage, seqs, q_host, o_host, wl.qh)
@@ -354,6 +354,9 @@ def e2e_decode(kv, wl: Decode, steps: int, warmup: int):
 
     ms_device = timed(step_device)
     ms = timed(step_host)
+    # What each call uploads besides Q: the lengths and the page-table entries
+    # that changed since the previous call (the table stays on the device).
+    table_bytes = kv.paged_attention_batch_table_upload_bytes(wl.storage)
     return ms, q_host.numel() * 4 + table_bytes, o_host.numel() * 4, ms_device
 
 

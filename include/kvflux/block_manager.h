@@ -79,6 +79,17 @@ public:
 
     Stats stats() const noexcept;
     std::size_t capacity() const noexcept { return slots_.size(); }
+    // Log of pages whose reference count fell to zero (the only way a handle
+    // that was live can go stale: its page must first lose every reference).
+    // zero_ref_events() counts such events since construction;
+    // zero_ref_ids_since(e, out) appends the ids of the events after the
+    // count was e, oldest first, and returns false (appending nothing) when
+    // more than kZeroLog of them happened since, i.e. the log cannot tell.
+    // A holder of handles checked when the count read e knows they are all
+    // still live if none of its ids is among them.
+    static constexpr std::size_t kZeroLog = 8192;
+    std::uint64_t zero_ref_events() const noexcept { return zero_events_; }
+    bool zero_ref_ids_since(std::uint64_t since, std::vector<std::size_t>& out) const;
     // Hint: bring the bookkeeping of `h` into cache ahead of a lookup. No
     // check, no effect on state.
     void prefetch(BlockHandle h) const noexcept {
@@ -123,6 +134,8 @@ private:
     std::size_t idle_oldest_ = kNone, idle_newest_ = kNone;
     std::size_t active_count_ = 0, idle_count_ = 0;
     std::unordered_map<std::uint64_t, std::vector<std::size_t>> index_;
+    std::vector<std::size_t> zero_log_;  // ring of kZeroLog ids
+    std::uint64_t zero_events_ = 0;
 };
 
 // Hot-path accessors, inline so page-table builds validate each entry cheaply.

@@ -5,6 +5,8 @@
 #include "kvflux/block_manager.h"
 
 #include <cstddef>
+#include <cstdint>
+#include <vector>
 
 namespace kvflux {
 
@@ -39,6 +41,12 @@ public:
     std::size_t block_size() const noexcept;
     // Pages that can be handed out now: free plus evictable idle cached pages.
     std::size_t available() const noexcept;
+    // The manager's log of pages whose references fell to zero
+    // (BlockManager::zero_ref_events / zero_ref_ids_since).
+    std::uint64_t zero_ref_events() const noexcept { return manager_.zero_ref_events(); }
+    bool zero_ref_ids_since(std::uint64_t since, std::vector<std::size_t>& out) const {
+        return manager_.zero_ref_ids_since(since, out);
+    }
 
 private:
     BlockManager manager_;

@@ -3,9 +3,19 @@
 // include/kvflux/v2/block_table.h:14-61). Entry i is logical block i; every
 // entry owns one reference in the PhysicalBlockPool and gives it back on
 // destruction, so the table is move-only.
+//
+// Beyond the reference's interface the table tracks its own changes, so that
+// a consumer keeping a copy of the ids (the device-resident page table of
+// paged_attention_batch) can refresh only what changed: lineage() names the
+// table's contents and is new after construction and after a move (both
+// ends), revision() is new after every edit that is not an append, and
+// first_changed_since() says from which entry on a copy taken at an earlier
+// revision may be out of date.
 #include "kvflux/physical_block_pool.h"
 
+#include <array>
 #include <cstddef>
+#include <cstdint>
 #include <vector>
 
 namespace kvflux::v2 {
@@ -34,11 +44,21 @@ public:
     PhysicalBlockID operator[](std::size_t logical_block) const {
         return physical_id(logical_block);
     }
-    // out[j] = physical_id(j) for every entry (the same checks and
-    // exceptions, in entry order), with the pool's bookkeeping of entry
-    // j + 32 prefetched while entry j is checked: entries are random pages,
-    // so one lookup after another would wait on a cache miss each.
-    void copy_ids(PhysicalBlockID* out) const;
+    // out[j - first] = physical_id(j) for entries j in [first, size()) (the
+    // same checks and exceptions, in entry order), with the pool's
+    // bookkeeping of entry j + 32 prefetched while entry j is checked:
+    // entries are random pages, so one lookup after another would wait on a
+    // cache miss each.
+    void copy_ids(PhysicalBlockID* out, std::size_t first = 0) const;
+
+    // Change tracking (see the file comment). Stamps come from one
+    // process-wide counter, so equal values always mean the same contents.
+    std::uint64_t lineage() const noexcept { return lineage_; }
+    std::uint64_t revision() const noexcept { return revision_; }
+    // Lowest entry index that may differ from what it held when revision()
+    // returned `revision` (an earlier value of this lineage): size() when
+    // only appends happened since, 0 when `revision` is too old to tell.
+    std::size_t first_changed_since(std::uint64_t revision) const noexcept;
     std::size_t size() const noexcept { return entries_.size(); }
     bool empty() const noexcept { return entries_.empty(); }
     bool shares_pool_with(const BlockTable& other) const noexcept {
@@ -55,21 +75,34 @@ public:
     void clear() noexcept;
 
 private:
+    // Records an edit of entries from `index` on (not an append).
+    void edited(std::size_t index) noexcept;
+
+    struct Edit {
+        std::uint64_t stamp;  // revision() after the edit
+        std::size_t index;    // lowest entry it touched
+    };
+    static constexpr std::size_t kEdits = 4;
+
     PhysicalBlockPool* pool_;  // null after being moved from
     std::vector<PhysicalBlockHandle> entries_;
+    std::uint64_t lineage_;
+    std::uint64_t revision_;
+    std::array<Edit, kEdits> edits_{};  // ring of the latest edits
+    std::uint64_t edit_count_ = 0;      // edits since the lineage began
 };
 
 inline PhysicalBlockID BlockTable::physical_id(std::size_t logical_block) const {
     return pool_->id(entries_.at(logical_block));  // generation-checked
 }
 
-inline void BlockTable::copy_ids(PhysicalBlockID* out) const {
+inline void BlockTable::copy_ids(PhysicalBlockID* out, std::size_t first) const {
     constexpr std::size_t kAhead = 32;
     const std::size_t n = entries_.size();
-    for (std::size_t j = 0; j < n && j < kAhead; ++j) pool_->prefetch(entries_[j]);
-    for (std::size_t j = 0; j < n; ++j) {
+    for (std::size_t j = first; j < n && j < first + kAhead; ++j) pool_->prefetch(entries_[j]);
+    for (std::size_t j = first; j < n; ++j) {
         if (j + kAhead < n) pool_->prefetch(entries_[j + kAhead]);
-        out[j] = pool_->id(entries_[j]);  // generation-checked
+        out[j - first] = pool_->id(entries_[j]);  // generation-checked
     }
 }
 

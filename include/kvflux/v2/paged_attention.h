@@ -12,6 +12,13 @@
 //   Q/O [num_sequences][query_heads][head_size].
 // Both are synchronous on the legacy default stream and validate shapes,
 // pointers and overlaps before launching.
+//
+// paged_attention_batch keeps the padded page table on the GPU between calls
+// (per storage): a call uploads the sequence lengths and only the table
+// entries that changed since the previous call (new pages, copied-on-write
+// pages, rows of sequences not in the previous batch) instead of the whole
+// table the reference uploads every call (src/v2/paged_attention.cu:287-292).
+// Stale or foreign handles still raise what build_batch_block_table raises.
 #include "kvflux/v2/paged_kv_storage.h"
 
 #include <cstddef>
@@ -39,6 +46,11 @@ void paged_attention_batch_host(const PagedKVStorage& storage,
                                 const std::vector<const SequenceState*>& sequences,
                                 const float* query_host, float* output_host,
                                 std::size_t query_heads);
+
+// Host->device bytes of tables and lengths the last paged_attention_batch(_host)
+// call on `storage` uploaded (Q of the _host form not included). No
+// counterpart in the reference.
+std::size_t paged_attention_batch_table_upload_bytes(const PagedKVStorage& storage);
 
 // paged_attention over several sequences of one storage in one call (a
 // prefill batch); no counterpart in the reference, whose callers make one

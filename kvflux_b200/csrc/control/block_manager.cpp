@@ -9,7 +9,8 @@
 namespace kvflux {
 
 BlockManager::BlockManager(std::size_t capacity, std::size_t block_size, Hasher hasher)
-    : slots_(capacity), meta_(capacity), block_size_(block_size), hasher_(std::move(hasher)) {
+    : slots_(capacity), meta_(capacity), block_size_(block_size), hasher_(std::move(hasher)),
+      zero_log_(kZeroLog) {
     if (capacity == 0 || block_size == 0 || !hasher_) {
         throw std::invalid_argument("block manager needs a positive capacity, block size and a hasher");
     }
@@ -93,6 +94,8 @@ void BlockManager::release(BlockHandle h) {
     Slot& s = live(h);
     if (s.refs == 0) throw std::invalid_argument("block has no reference to release");
     if (--s.refs != 0) return;
+    zero_log_[zero_events_ % kZeroLog] = h.id;
+    ++zero_events_;
     --active_count_;
     if (s.published) {
         s.state = State::Idle;
@@ -218,6 +221,13 @@ BlockHandle BlockManager::block_at(const BlockTable& table, std::size_t token_in
     const BlockHandle h = table.blocks.at(token_index / block_size_);
     if (live(h).refs == 0) throw std::invalid_argument("block table entry not held");
     return h;
+}
+
+bool BlockManager::zero_ref_ids_since(std::uint64_t since, std::vector<std::size_t>& out) const {
+    if (since > zero_events_) return false;
+    if (zero_events_ - since > kZeroLog) return false;
+    for (std::uint64_t e = since; e < zero_events_; ++e) out.push_back(zero_log_[e % kZeroLog]);
+    return true;
 }
 
 BlockManager::Stats BlockManager::stats() const noexcept {

@@ -2,7 +2,6 @@
 // (src/v2/paged_attention.cu:193-313) in the same check order; the kernels
 // are reached through kvfx_attention / kvfx_decode.
 #include <algorithm>
-#include <atomic>
 #include <cstring>
 #include <limits>
 
@@ -214,42 +213,9 @@ void batch_decode(const PagedKVStorage& storage, const std::vector<const Sequenc
 
     detail::DeviceGuard guard(storage.device());
     detail::StorageRuntime& rt = storage.runtime();
-    // Staging: the lengths, then the padded table, so that a prefix of rows
-    // and the lengths go up in one copy.
-    void* host[2] = {nullptr, nullptr};
-    void* dev[2] = {nullptr, nullptr};
-    const std::size_t bytes[2] = {lengths_bytes, table_bytes};
-    rt.stage(bytes, 2, host, dev);
-    auto* table = static_cast<PhysicalBlockID*>(host[1]);
-    const std::size_t table_offset =
-        static_cast<std::size_t>(static_cast<unsigned char*>(host[1]) - static_cast<unsigned char*>(host[0]));
-    const std::size_t row_bytes = widest * sizeof(PhysicalBlockID);
-    const std::size_t num_blocks = layout.num_blocks();
+    (void)table_bytes;
+    (void)lengths_bytes;
 
-    // Rows [r0, r1) of the table, written in parallel, page ids range-checked
-    // as they are written. Any exception from the control plane is reproduced
-    // by the sequential build, so that the first failing row raises it.
-    auto fill_rows = [&](std::size_t r0, std::size_t r1) {
-        std::atomic<bool> bad{false};
-        try {
-            detail::parallel_for(r1 - r0, 4, [&](std::size_t i0, std::size_t i1) {
-                bool out_of_range = false;
-                for (std::size_t r = r0 + i0; r < r0 + i1; ++r) {
-                    PhysicalBlockID* row = table + r * widest;
-                    const SequenceState& s = *sequences[r];
-                    const std::size_t n = s.num_allocated_blocks();
-                    s.copy_physical_block_ids(row);
-                    for (std::size_t j = 0; j < n; ++j) out_of_range |= row[j] >= num_blocks;
-                    std::fill(row + n, row + widest, BatchBlockTable::invalid_block());
-                }
-                if (out_of_range) bad.store(true, std::memory_order_relaxed);
-            });
-        } catch (...) {
-            (void)build_batch_block_table(sequences);
-            throw;
-        }
-        if (bad.load()) throw std::out_of_range("batch attention block out of range");
-    };
     auto check_pointers = [&] {
         const std::size_t elements = detail::mul_checked(
             detail::mul_checked(batch, query_heads, "batch attention"), layout.head_size(), "batch attention");
@@ -284,11 +250,17 @@ void batch_decode(const PagedKVStorage& storage, const std::vector<const Sequenc
         pointers_ok = false;
     }
     if (!pointers_ok) {
-        fill_rows(0, batch);
+        (void)build_batch_block_table(sequences);
         check_pointers();
     }
 
-    std::memcpy(host[0], lens.data(), lengths_bytes);
+    // The page table stays on the device between calls; this uploads the
+    // lengths and whatever entries changed (one copy, one patch launch).
+    const detail::ResidentTable::View table = rt.batch_table.refresh(rt, sequences, lens, widest, layout.num_blocks());
+    rt.last_table_upload = table.h2d_bytes;
+    const std::size_t width = table.width;
+    const std::size_t row_bytes = width * sizeof(PhysicalBlockID);
+
     const std::size_t max_len = *std::max_element(lens.begin(), lens.end());
     std::size_t total = 0;
     for (const std::size_t l : lens) total += l;
@@ -322,56 +294,32 @@ void batch_decode(const PagedKVStorage& storage, const std::vector<const Sequenc
     auto launch_rows = [&](std::size_t r0, std::size_t r1, void* ws, std::size_t ws_bytes, cudaStream_t stream) {
         detail::check_kvfx(
             kvfx_decode(&rt.cache, q_dev + r0 * row_elems, o_dev + r0 * row_elems,
-                        reinterpret_cast<const uint64_t*>(static_cast<unsigned char*>(dev[1]) + r0 * row_bytes),
-                        static_cast<const uint64_t*>(dev[0]) + r0, r1 - r0, widest, qh, chunk_max(r0, r1), pps,
-                        ws, ws_bytes, stream),
+                        reinterpret_cast<const uint64_t*>(reinterpret_cast<const unsigned char*>(table.table) +
+                                                          r0 * row_bytes),
+                        table.lens + r0, r1 - r0, width, qh, chunk_max(r0, r1), pps, ws, ws_bytes, stream),
             "paged attention batch");
     };
 
-    // Rows go to the GPU in two chunks. The kernel over the first quarter
-    // starts after a quarter of the host's table writing; meanwhile the host
-    // writes the rest, and a side stream uploads it and runs the second
-    // kernel concurrently with the first, on its own workspace, so that its
-    // CTAs take the SMs the first kernel's last CTAs leave idle. Measured on
-    // B200 at 256 rows of 4K-32K tokens: the first kernel lasts ~0.7 ms,
-    // enough to cover the rest of the table (~0.2 ms of host writing, then
-    // ~0.3 ms of upload while the kernel saturates HBM), and the two kernels
-    // take as long as one launch over every row.
-    // With host I/O the first chunk also waits for its Q upload (measured at
-    // config 5 per call: a quarter of the rows first 2.80-2.92 ms, a third
-    // 2.85, a half 3.08, an eighth 2.96; with the second chunk's Q issued
-    // before the first chunk's table, 2.85; three chunks - a sixteenth on the
-    // default stream, the rest of the first quarter on the side stream, the
-    // last three quarters on the default stream after the first kernel -
-    // 2.89).
-    const std::size_t head_rows = batch >= 16 ? (batch + 3) / 4 : batch;
+    // Device Q: one launch over every row. Host Q: two chunks, so that the
+    // kernel over the first quarter of the rows starts once its Q is up
+    // while the rest of Q goes up on a side stream, whose launch over the
+    // other rows (own workspace, same split size) then runs concurrently
+    // and fills the SMs the first kernel's last CTAs leave idle.
+    const std::size_t head_rows = host_io && batch >= 16 ? (batch + 3) / 4 : batch;
     const std::size_t ws0 = workspace_of(0, head_rows);
     const std::size_t ws1 = head_rows < batch ? workspace_of(head_rows, batch) : 0;
     auto* ws = static_cast<unsigned char*>(rt.ensure_workspace(ws0 + ws1));
     upload_q(0, head_rows, nullptr);
     if (head_rows < batch) {
         // The side stream does not wait for the default stream by itself:
-        // order it after the caller's work (Q) issued before this call.
+        // order it after the table patch and the caller's earlier work.
         rt.ensure_side();
         detail::cuda_check(cudaEventRecord(rt.side_ready, nullptr), "record side start");
         detail::cuda_check(cudaStreamWaitEvent(rt.side, rt.side_ready, 0), "order side start");
     }
-    fill_rows(0, head_rows);
-    rt.push_range(0, table_offset + head_rows * row_bytes, nullptr);
     launch_rows(0, head_rows, ws0 ? ws : nullptr, ws0, nullptr);
-    // Issued after the first chunk's table, which would otherwise queue
-    // behind it on the copy engine.
-    if (head_rows < batch) upload_q(head_rows, batch, rt.side);
     if (head_rows < batch) {
-        try {
-            fill_rows(head_rows, batch);
-        } catch (...) {
-            // Raised only by a pool inconsistent with its sequences; the rows
-            // already launched finish before the staging can be reused.
-            (void)cudaStreamSynchronize(nullptr);
-            throw;
-        }
-        rt.push_range(table_offset + head_rows * row_bytes, (batch - head_rows) * row_bytes, rt.side);
+        upload_q(head_rows, batch, rt.side);
         launch_rows(head_rows, batch, ws1 ? ws + ws0 : nullptr, ws1, rt.side);
         detail::cuda_check(cudaEventRecord(rt.side_done, rt.side), "record side work");
         detail::cuda_check(cudaStreamWaitEvent(nullptr, rt.side_done, 0), "order side work");
@@ -389,6 +337,10 @@ void paged_attention_batch(const PagedKVStorage& storage, const std::vector<cons
 void paged_attention_batch_host(const PagedKVStorage& storage, const std::vector<const SequenceState*>& sequences,
                                 const float* query_host, float* output_host, std::size_t query_heads) {
     batch_decode(storage, sequences, query_host, output_host, query_heads, true);
+}
+
+std::size_t paged_attention_batch_table_upload_bytes(const PagedKVStorage& storage) {
+    return storage.runtime().last_table_upload;
 }
 
 } // namespace kvflux::v2

@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "kvflux/v2/paged_kv_storage.h"
+#include "kvflux/v2/sequence_state.h"
 #include "kvfx.h"
 
 namespace kvflux::v2::detail {
@@ -43,6 +44,73 @@ private:
 // invalid_argument unless `p` is device memory (cudaMemoryTypeDevice) of `device`.
 void require_device_pointer(const void* p, int device, const char* name);
 bool overlaps(const void* a, std::size_t a_bytes, const void* b, std::size_t b_bytes);
+
+// One run of a table patch: ids[src, src + count) go to table[dst, dst + count).
+struct TablePatchRun {
+    uint64_t dst;
+    uint64_t src;
+    uint64_t count;
+};
+// Enqueues the copy of every run (table, runs and ids are device memory).
+cudaError_t launch_table_patch(uint64_t* table, const TablePatchRun* runs, const uint64_t* ids, uint32_t num_runs,
+                               cudaStream_t stream);
+
+struct StorageRuntime;
+
+// The device-resident copy of the padded [rows][width] page table of the last
+// batch decode on a storage (reference: build_batch_block_table,
+// src/v2/batch_block_table.cpp:18-48, whose table paged_attention_batch
+// uploads whole on every call, src/v2/paged_attention.cu:287-292). Each call
+// re-reads, checks and uploads only the entries that changed since the last
+// call: a row is keyed by its BlockTable's lineage and revision, so a row that
+// only grew re-reads its new entries and an unchanged row re-reads nothing.
+// Unchanged entries need no generation re-check unless one of their pages
+// lost its last reference since (the pool's zero-reference log): that is the
+// only way a handle checked earlier can go stale, so only then is every row
+// re-checked, in row order, raising what build_batch_block_table would.
+class ResidentTable {
+public:
+    ResidentTable() = default;
+    ~ResidentTable();
+    ResidentTable(const ResidentTable&) = delete;
+    ResidentTable& operator=(const ResidentTable&) = delete;
+
+    struct View {
+        const uint64_t* table;  // device [rows][width]
+        std::size_t width;      // row stride in entries (>= every row's pages)
+        const uint64_t* lens;   // device [rows]: num_tokens of each row
+        std::size_t h2d_bytes;  // bytes uploaded by this refresh
+    };
+    // Brings the device table up to date with `sequences` (already checked to
+    // share one pool and to have `lens[r]` tokens and at most `widest` pages)
+    // and uploads the lengths, all through rt's staging with one copy and at
+    // most one patch launch on the legacy default stream. Throws what
+    // build_batch_block_table throws for a stale handle and out_of_range for
+    // an id outside the storage; after any exception the copy is forgotten.
+    View refresh(StorageRuntime& rt, const std::vector<const SequenceState*>& sequences,
+                 const std::vector<std::size_t>& lens, std::size_t widest, std::size_t num_blocks);
+    // Forgets the copy: the next refresh re-reads every row.
+    void invalidate() noexcept;
+
+private:
+    struct RowKey {
+        std::uint64_t lineage = 0;
+        std::uint64_t revision = 0;
+        std::size_t count = 0;
+    };
+    void unhold(std::size_t row, std::size_t from) noexcept;
+
+    uint64_t* dev_ = nullptr;
+    int device_ = -1;
+    std::size_t rows_cap_ = 0, width_ = 0;
+    std::vector<RowKey> rows_;                 // rows currently held
+    std::vector<PhysicalBlockID> mirror_;      // host copy [rows_cap_][width_]
+    std::vector<std::uint32_t> holders_;       // per page id: held entries naming it
+    const PhysicalBlockPool* pool_ = nullptr;
+    std::uint64_t zero_events_ = 0;            // pool's zero-reference count when last checked
+    std::vector<std::size_t> released_;        // scratch: ids from the zero-reference log
+    std::vector<std::size_t> dirty_from_;      // scratch: per row, first entry to re-read
+};
 
 struct StorageRuntime {
     kvfx_cache cache{};
@@ -94,6 +162,10 @@ struct StorageRuntime {
     void* ensure_io(std::size_t bytes);
     // Synchronises the legacy default stream and raises on device-side flags.
     void finish(const char* op) const;
+    // Device-resident page table of paged_attention_batch(_host), and the
+    // bytes its last refresh uploaded (tables and lengths).
+    ResidentTable batch_table;
+    std::size_t last_table_upload = 0;
 };
 
 // Runs fn(begin, end) over [0, n) in chunks of `grain` on a small pool of

@@ -114,7 +114,13 @@ PYBIND11_MODULE(_C, m) {
         .def("ref_count", &PhysicalBlockPool::ref_count)
         .def("capacity", &PhysicalBlockPool::capacity)
         .def("block_size", &PhysicalBlockPool::block_size)
-        .def("available", &PhysicalBlockPool::available);
+        .def("available", &PhysicalBlockPool::available)
+        .def("zero_ref_events", &PhysicalBlockPool::zero_ref_events)
+        .def("zero_ref_ids_since", [](const PhysicalBlockPool& p, std::uint64_t since) -> py::object {
+            std::vector<std::size_t> ids;
+            if (!p.zero_ref_ids_since(since, ids)) return py::none();
+            return py::cast(ids);
+        });
     m.def("prefix_hash", &BlockManager::prefix_hash);
 
     py::class_<BlockTable>(m, "BlockTable")
@@ -134,6 +140,9 @@ PYBIND11_MODULE(_C, m) {
         .def("pop_back", &BlockTable::pop_back)
         .def("replace_last_owned", &BlockTable::replace_last_owned)
         .def("clear", &BlockTable::clear)
+        .def("lineage", &BlockTable::lineage)
+        .def("revision", &BlockTable::revision)
+        .def("first_changed_since", &BlockTable::first_changed_since)
         .def("move_from", [](BlockTable& self, BlockTable& other) { self = std::move(other); });
 
     py::class_<TokenLocation>(m, "TokenLocation")
@@ -242,6 +251,7 @@ PYBIND11_MODULE(_C, m) {
                                            py::object q, py::object o, std::size_t query_heads) {
         paged_attention_batch_host(s, seqs, ptr<const float>(q), ptr<float>(o), query_heads);
     });
+    m.def("paged_attention_batch_table_upload_bytes", &paged_attention_batch_table_upload_bytes);
     m.def("paged_attention_prefill_batch",
           [](const PagedKVStorage& s, const std::vector<const SequenceState*>& seqs, const py::list& qs,
              const py::list& os, const std::vector<std::size_t>& query_tokens, std::size_t query_heads) {

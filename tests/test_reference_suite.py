@@ -19,6 +19,9 @@ import importlib.util  # noqa: E402
 _spec = importlib.util.spec_from_file_location("reference_suite_build", HERE / "reference_suite" / "build.py")
 _suite = importlib.util.module_from_spec(_spec)
 _spec.loader.exec_module(_suite)
+# Where a KVFlux checkout is found, bring the programs up to date with the
+# current headers and library first (incremental); elsewhere run what was built.
+_suite.build()
 
 
 def _run(name: str, timeout: int = 300) -> None:
