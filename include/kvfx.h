@@ -134,10 +134,14 @@ int kvfx_copy_page(const kvfx_cache* cache, uint64_t src_block, uint64_t dst_blo
  *   seq_lens     : device uint64[batch], each in [1, max_seq_len]
  *   max_seq_len  : host-side upper bound of seq_lens (sizes the grid)
  *   pages_per_split: split-K chunk in pages; 0 chooses one from the shape
- *   workspace    : device scratch of kvfx_decode_workspace_bytes(...) bytes;
- *                  any contents (each launch clears the split counters it
- *                  uses on `stream` before the kernel), reusable for any
- *                  shape once the launch that used it has completed.
+ *   workspace    : device scratch of kvfx_decode_workspace_bytes(...) bytes,
+ *                  zero-filled (cudaMemset) before its first use. Its start
+ *                  holds the split counters, which every launch leaves at
+ *                  zero again, so it stays ready for the next launch of any
+ *                  batch, lengths or split size on caches with the same
+ *                  num_kv_heads (zero it again before using it with a cache
+ *                  of another head count). Launches that share a workspace
+ *                  must not overlap on the GPU.
  * q_heads must be a multiple of num_kv_heads; Q head j uses KV head
  * j / (q_heads / num_kv_heads). Scale 1/sqrt(head_size).
  * Replaces paged_attention_batch's launch (KVFlux src/v2/paged_attention.cu:248-313).
@@ -191,9 +195,14 @@ int kvfx_decode_append(const kvfx_cache* cache, const void* k_new, const void* v
  * size is chosen so the scratch fits, and a batch whose batch x num_kv_heads
  * cannot fit even with one split per sequence is rejected with KVFX_ENOSPACE.
  * The first call on a device looks up the array's address (make it before
- * any stream capture). All calls share the array: calls that overlap on the
- * GPU race; each call clears the counters it uses. Device-side index/timeout
- * flags are not recorded for this entry point.
+ * any stream capture; a device reset invalidates it, so do not call this on
+ * a device after resetting it). All calls share the array: calls that
+ * overlap on the GPU race. The split counters return to zero at the end of
+ * every launch; the first call on a device, and a call whose cache has
+ * another num_kv_heads than the previous call's, clears them on `stream`
+ * first. Device-side flags (an out-of-range page id, a bounded wait that
+ * gave up) are kept in a device variable that kvfx_device_status reads
+ * together with the other kernels' flags.
  */
 int kvfx_decode_noalloc(const kvfx_cache* cache, const float* q, float* o,
                         const uint64_t* block_table, const uint64_t* seq_lens, uint64_t batch,
@@ -204,7 +213,9 @@ int kvfx_decode_noalloc(const kvfx_cache* cache, const float* q, float* o,
  * Single-sequence causal PagedAttention with query_tokens queries aligned to
  * the end of the kv_tokens-long sequence (query i sees positions
  * <= kv_tokens - query_tokens + i). q, o: device float[query_tokens][q_heads][head_size];
- * blocks: device uint64[ceil(kv_tokens / bs)].
+ * blocks: device uint64[ceil(kv_tokens / bs)]. workspace: as for kvfx_decode
+ * (zero-filled before its first use; query_tokens == 1 runs the decode
+ * kernel, the only case that needs one).
  * Replaces paged_attention's launch (KVFlux src/v2/paged_attention.cu:193-246).
  */
 uint64_t kvfx_attention_workspace_bytes(const kvfx_cache* cache, uint64_t query_tokens,
@@ -238,8 +249,8 @@ const char* kvfx_last_error(void);
 
 /*
  * Reads the status word of `device` (KVFX_FLAG_* bits set by kernels since
- * the last clear) after the caller has synchronised the work in question;
- * clears it when `clear` is non-zero.
+ * the last clear, kvfx_decode_noalloc's included) after the caller has
+ * synchronised the work in question; clears it when `clear` is non-zero.
  */
 int kvfx_device_status(int device, uint32_t* flags, int clear);
 

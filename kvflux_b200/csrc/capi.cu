@@ -125,6 +125,13 @@ int kvfx_device_status(int device, uint32_t* flags, int clear) {
     volatile unsigned* vw = w;  // mapped host memory: host and device views coincide (UVA)
     *flags = *vw;
     if (clear) *vw = 0;
+    // kvfx_decode_noalloc's launches keep their flags in a device variable
+    // (that entry point allocates nothing, not even this mapped word).
+    unsigned extra = 0;
+    if (!kvfx::noalloc_status(device, &extra, clear != 0)) {
+        return fail(KVFX_ECUDA, "reading the no-allocation decode's status word failed");
+    }
+    *flags |= extra;
     return KVFX_OK;
 }
 

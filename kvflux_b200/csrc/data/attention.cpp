@@ -308,7 +308,8 @@ void batch_decode(const PagedKVStorage& storage, const std::vector<const Sequenc
     const std::size_t head_rows = host_io && batch >= 16 ? (batch + 3) / 4 : batch;
     const std::size_t ws0 = workspace_of(0, head_rows);
     const std::size_t ws1 = head_rows < batch ? workspace_of(head_rows, batch) : 0;
-    auto* ws = static_cast<unsigned char*>(rt.ensure_workspace(ws0 + ws1));
+    void* ws_head = rt.ensure_workspace(ws0, 0);
+    void* ws_rest = rt.ensure_workspace(ws1, 1);
     upload_q(0, head_rows, nullptr);
     if (head_rows < batch) {
         // The side stream does not wait for the default stream by itself:
@@ -317,10 +318,10 @@ void batch_decode(const PagedKVStorage& storage, const std::vector<const Sequenc
         detail::cuda_check(cudaEventRecord(rt.side_ready, nullptr), "record side start");
         detail::cuda_check(cudaStreamWaitEvent(rt.side, rt.side_ready, 0), "order side start");
     }
-    launch_rows(0, head_rows, ws0 ? ws : nullptr, ws0, nullptr);
+    launch_rows(0, head_rows, ws_head, rt.workspace_size(0), nullptr);
     if (head_rows < batch) {
         upload_q(head_rows, batch, rt.side);
-        launch_rows(head_rows, batch, ws1 ? ws + ws0 : nullptr, ws1, rt.side);
+        launch_rows(head_rows, batch, ws_rest, rt.workspace_size(1), rt.side);
         detail::cuda_check(cudaEventRecord(rt.side_done, rt.side), "record side work");
         detail::cuda_check(cudaStreamWaitEvent(nullptr, rt.side_done, 0), "order side work");
     }

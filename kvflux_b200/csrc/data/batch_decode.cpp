@@ -284,7 +284,8 @@ std::vector<TokenLocation> BatchDecodeSession::step_host(const void* key_host, c
         };
         const std::size_t ws0 = ws_of(0, head_rows);
         const std::size_t ws1 = head_rows < batch ? ws_of(head_rows, batch) : 0;
-        auto* ws = static_cast<unsigned char*>(rt.ensure_workspace(ws0 + ws1));
+        void* ws_head = rt.ensure_workspace(ws0, 0);
+        void* ws_rest = rt.ensure_workspace(ws1, 1);
         auto launch = [&](std::size_t r0, std::size_t r1, void* w, std::size_t wb, cudaStream_t st) {
             detail::check_kvfx(
                 kvfx_decode_append(&rt.cache, k_dev + r0 * kv_row, v_dev + r0 * kv_row, slots_d + r0,
@@ -301,10 +302,10 @@ std::vector<TokenLocation> BatchDecodeSession::step_host(const void* key_host, c
             detail::cuda_check(cudaEventRecord(rt.side_ready, nullptr), "record side start");
             detail::cuda_check(cudaStreamWaitEvent(rt.side, rt.side_ready, 0), "order side start");
         }
-        launch(0, head_rows, ws0 ? ws : nullptr, ws0, nullptr);
+        launch(0, head_rows, ws_head, rt.workspace_size(0), nullptr);
         if (head_rows < batch) {
             upload(head_rows, batch, rt.side);
-            launch(head_rows, batch, ws1 ? ws + ws0 : nullptr, ws1, rt.side);
+            launch(head_rows, batch, ws_rest, rt.workspace_size(1), rt.side);
             detail::cuda_check(cudaEventRecord(rt.side_done, rt.side), "record side work");
             detail::cuda_check(cudaStreamWaitEvent(nullptr, rt.side_done, 0), "order side work");
         }

@@ -123,10 +123,15 @@ struct StorageRuntime {
     void* pinned = nullptr;
     std::size_t pinned_bytes = 0;
 
-    // Decode/attention workspace, zero-filled when (re)allocated; the kernels
-    // leave it reusable.
+    // Decode/attention workspaces, zero-filled when (re)allocated; the
+    // kernels leave them reusable (the decode's split counters sit at the
+    // start of each and return to zero at the end of every launch). Slot 0
+    // serves single launches and the first of two concurrent chunks, slot 1
+    // the second chunk, so each counter region stays where it was.
     void* workspace = nullptr;
     std::size_t workspace_bytes = 0;
+    void* workspace2 = nullptr;
+    std::size_t workspace2_bytes = 0;
 
     // One bit per slot for the duplicate check of write_paged_kv.
     std::vector<std::uint64_t> seen;
@@ -154,7 +159,9 @@ struct StorageRuntime {
     cudaStream_t side = nullptr;
     cudaEvent_t side_ready = nullptr;
     cudaEvent_t side_done = nullptr;
-    void* ensure_workspace(std::size_t bytes);
+    // Workspace of `slot` (0 or 1) with at least `bytes`, or nullptr for 0 bytes.
+    void* ensure_workspace(std::size_t bytes, int slot = 0);
+    std::size_t workspace_size(int slot = 0) const { return slot == 0 ? workspace_bytes : workspace2_bytes; }
     // Device buffer for inputs staged from the caller's host memory (Q of
     // paged_attention_batch_host); grows, never shrinks.
     void* io = nullptr;

@@ -59,6 +59,7 @@ StorageRuntime::~StorageRuntime() {
     if (cudaSetDevice(device) != cudaSuccess) return;
     if (dev_scratch) (void)cudaFree(dev_scratch);
     if (workspace) (void)cudaFree(workspace);
+    if (workspace2) (void)cudaFree(workspace2);
     if (io) (void)cudaFree(io);
     if (pinned) (void)cudaFreeHost(pinned);
     if (side_ready) (void)cudaEventDestroy(side_ready);
@@ -131,17 +132,19 @@ void StorageRuntime::upload(const void* const* host, const std::size_t* bytes, i
     push();
 }
 
-void* StorageRuntime::ensure_workspace(std::size_t bytes) {
+void* StorageRuntime::ensure_workspace(std::size_t bytes, int slot) {
     if (bytes == 0) return nullptr;
-    if (bytes > workspace_bytes) {
-        if (workspace) cuda_check(cudaFree(workspace), "free workspace");
-        workspace = nullptr;
-        workspace_bytes = 0;
-        cuda_check(cudaMalloc(&workspace, bytes), "allocate workspace");
-        cuda_check(cudaMemsetAsync(workspace, 0, bytes, nullptr), "clear workspace");
-        workspace_bytes = bytes;
+    void*& ptr = slot == 0 ? workspace : workspace2;
+    std::size_t& size = slot == 0 ? workspace_bytes : workspace2_bytes;
+    if (bytes > size) {
+        if (ptr) cuda_check(cudaFree(ptr), "free workspace");
+        ptr = nullptr;
+        size = 0;
+        cuda_check(cudaMalloc(&ptr, bytes), "allocate workspace");
+        cuda_check(cudaMemsetAsync(ptr, 0, bytes, nullptr), "clear workspace");
+        size = bytes;
     }
-    return workspace;
+    return ptr;
 }
 
 void* StorageRuntime::ensure_io(std::size_t bytes) {

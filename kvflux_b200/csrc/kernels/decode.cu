@@ -22,9 +22,11 @@
 // -inf in the scores and zeroed in the V tile (0 * garbage must not reach O).
 //
 // Split merge: a split writes (max, sum, unnormalised O) to the workspace and
-// bumps a per-(request, head) counter; the CTA that completes the count merges
-// all splits with log-sum-exp weights and writes O. The counters are cleared
-// on the stream before each launch. No CTA ever waits for another.
+// bumps a per-(request, head) counter; the CTA that completes the count resets
+// the counter to zero, merges all splits with log-sum-exp weights and writes
+// O. No CTA ever waits for another, and a workspace zero-filled once needs no
+// clearing between launches (a CTA whose loads timed out still counts itself,
+// with a split that contributes nothing, so every count completes).
 //
 // Append mode (one decode step fused with its paged KV write): each row's new
 // token is the last position; the CTA whose split holds that page writes the
@@ -32,6 +34,7 @@
 // memory tiles, and takes the page from the token's slot, so the launch needs
 // neither a separate write kernel nor a host update of the table.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 
 #include "common.cuh"
@@ -325,27 +328,32 @@ decode_mma_kernel(const __grid_constant__ DecodeParams p, const __grid_constant_
     __syncthreads();
     if (!ok) s_flag = 1;
     __syncthreads();
-    if (s_flag != 0) return;  // a load never arrived: status already flagged
+    // A load never arrived (status already flagged): no O from this CTA; a
+    // split still counts itself with an empty partial (below).
+    const bool failed = s_flag != 0;
+    if (failed && nsplits == 1) return;
 
     float* mo = reinterpret_cast<float*>(smem);  // [kWarps][8][HD]
-    if (live) {
-        float* dst = mo + (warp * 8 + g) * HD;
+    if (!failed) {
+        if (live) {
+            float* dst = mo + (warp * 8 + g) * HD;
 #pragma unroll
-        for (int n = 0; n < S::kNTiles; ++n) {
-            *reinterpret_cast<float2*>(dst + 8 * n + 2 * tig) =
-                make_float2(oacc[n][0] + oacc[n][2], oacc[n][1] + oacc[n][3]);
+            for (int n = 0; n < S::kNTiles; ++n) {
+                *reinterpret_cast<float2*>(dst + 8 * n + 2 * tig) =
+                    make_float2(oacc[n][0] + oacc[n][2], oacc[n][1] + oacc[n][3]);
+            }
+            if (tig == 0) {
+                s_m[warp][g] = m_run;
+                s_l[warp][g] = l_run;
+            }
+        } else if (tig == 0) {
+            s_m[warp][g] = -INFINITY;
+            s_l[warp][g] = 0.f;
         }
-        if (tig == 0) {
-            s_m[warp][g] = m_run;
-            s_l[warp][g] = l_run;
-        }
-    } else if (tig == 0) {
-        s_m[warp][g] = -INFINITY;
-        s_l[warp][g] = 0.f;
     }
     __syncthreads();
     const uint32_t G = p.group;
-    if (tid < static_cast<int>(G)) {
+    if (!failed && tid < static_cast<int>(G)) {
         float M = -INFINITY;
         for (int w = 0; w < kWarps; ++w) M = fmaxf(M, s_m[w][tid]);
         float L = 0.f;
@@ -376,19 +384,26 @@ decode_mma_kernel(const __grid_constant__ DecodeParams p, const __grid_constant_
     for (uint32_t idx = tid; idx < G * HD; idx += kWarps * 32) {
         const uint32_t gg = idx / HD, d = idx - gg * HD;
         float acc = 0.f;
+        if (!failed) {
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) acc += mo[(w * 8 + gg) * HD + d] * s_scale[w][gg];
+            for (int w = 0; w < kWarps; ++w) acc += mo[(w * 8 + gg) * HD + d] * s_scale[w][gg];
+        }
         part[gg * (HD + 2) + d] = acc;
     }
     if (tid < static_cast<int>(G)) {
-        part[tid * (HD + 2) + HD] = s_m[0][tid];
-        part[tid * (HD + 2) + HD + 1] = s_l[0][tid];
+        part[tid * (HD + 2) + HD] = failed ? -INFINITY : s_m[0][tid];
+        part[tid * (HD + 2) + HD + 1] = failed ? 0.f : s_l[0][tid];
     }
     __threadfence();
     __syncthreads();
     if (tid == 0) {
-        const unsigned prev = atomicAdd(p.counters + pair, 1u);
-        s_flag = prev == nsplits - 1 ? 2 : 0;
+        // 16-bit counters, two per word; nsplits <= 256 never carries.
+        unsigned* word = p.counters + (pair >> 1);
+        const unsigned shift = static_cast<unsigned>(pair & 1u) * 16u;
+        const unsigned prev = (atomicAdd(word, 1u << shift) >> shift) & 0xffffu;
+        const bool last = prev == nsplits - 1;
+        if (last) atomicSub(word, nsplits << shift);  // zero again for the next launch
+        s_flag = last ? 2 : 0;
     }
     __syncthreads();
     if (s_flag != 2) return;
@@ -461,12 +476,13 @@ template <int HD, typename T>
 cudaError_t launch_fast(const CacheView& c, const DecodeArgs& a, const CacheMaps* maps, uint32_t pps,
                         uint32_t max_splits, unsigned* status, cudaStream_t s) {
     using Sh = Shape<HD>;
-    static int attr_done[64] = {0};
-    if (c.device >= 0 && c.device < 64 && !attr_done[c.device]) {
+    static std::atomic<int> attr_done[64];  // zero-initialised (static storage)
+    if (c.device < 0 || c.device >= 64 || !attr_done[c.device].load(std::memory_order_acquire)) {
+        // Idempotent: threads that race here all set the same attribute.
         cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<HD, T>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::kSmem);
         if (e != cudaSuccess) return e;
-        attr_done[c.device] = 1;
+        if (c.device >= 0 && c.device < 64) attr_done[c.device].store(1, std::memory_order_release);
     }
     DecodeParams p;
     p.q = a.q;
@@ -481,10 +497,8 @@ cudaError_t launch_fast(const CacheView& c, const DecodeArgs& a, const CacheMaps
     p.pages_per_split = pps;
     p.max_splits = max_splits;
     p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.hd)));
-    p.partial = static_cast<float*>(a.workspace);
-    const uint64_t pbytes =
-        ((a.batch * c.heads * max_splits * static_cast<uint64_t>(Sh::kPartial) * 4) + 255) & ~uint64_t(255);
-    p.counters = reinterpret_cast<unsigned*>(static_cast<char*>(a.workspace) + pbytes);
+    p.counters = static_cast<unsigned*>(a.workspace);
+    p.partial = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + decode_counter_bytes(c.heads));
     p.status = status;
     p.k_new = a.k_new;
     p.v_new = a.v_new;
@@ -492,13 +506,6 @@ cudaError_t launch_fast(const CacheView& c, const DecodeArgs& a, const CacheMaps
     p.table_out = a.table_out;
     p.k_base = c.k;
     p.v_base = c.v;
-    if (max_splits > 1) {
-        // The split counters start at zero on the launch's stream. Their
-        // offset follows (batch, max_splits), so in a workspace reused with
-        // another shape they lie where earlier partials were written.
-        const cudaError_t e = cudaMemsetAsync(p.counters, 0, a.batch * c.heads * sizeof(unsigned), s);
-        if (e != cudaSuccess) return e;
-    }
     dim3 grid(max_splits, c.heads, static_cast<uint32_t>(a.batch));
     decode_mma_kernel<HD, T><<<grid, kWarps * 32, Sh::kSmem, s>>>(p, maps->k, maps->v);
     return cudaGetLastError();
@@ -540,7 +547,7 @@ uint64_t decode_workspace_bytes(const CacheView& c, uint64_t batch, uint32_t q_h
     const uint64_t max_splits = ceil_div(ceil_div(std::max<uint64_t>(max_len, 1), c.bs), pps);
     const uint64_t per = 8ull * (c.hd + 2);
     const uint64_t pbytes = ((batch * c.heads * max_splits * per * 4) + 255) & ~uint64_t(255);
-    return pbytes + batch * c.heads * 4;
+    return decode_counter_bytes(c.heads) + pbytes;
 }
 
 cudaError_t launch_decode(const CacheView& c, const DecodeArgs& a, unsigned* status, cudaStream_t s) {

@@ -13,12 +13,20 @@
 // The array is kNoAllocScratchBytes (16 MiB) of device memory on every GPU
 // where this module is loaded (with CUDA's lazy module loading, the GPUs on
 // which this entry point has run), held until the process exits. Its device
-// address is looked up once per device (cudaGetSymbolAddress, with that
-// device current) on the first call made on that device; make that first call
-// before any stream capture. Every call shares the one array and it keeps the
-// previous call's contents: each call clears the counters it uses, and calls
-// that overlap on the GPU (on different streams, or from different threads
-// without ordering) race on it.
+// address, and that of a status word beside it, are looked up once per device
+// (cudaGetSymbolAddress, with that device current) on the first call made on
+// that device; make that first call before any stream capture. The addresses
+// are kept for the life of the process: a device reset (cudaDeviceReset) or
+// a torn-down context invalidates them, so an embedder that resets a device
+// must not call this entry point on it afterwards. Every call
+// shares the one array and it keeps the previous call's contents: the split
+// counters at its start return to zero at the end of every launch, and are
+// cleared on the call's stream by the first call on a device and by a call
+// whose cache has a different number of KV heads than the previous call's
+// (the counters' region depends on it); calls that overlap on the GPU (on
+// different streams, or from different threads without ordering) race on the
+// array. Device-side flags (an out-of-range page id, a bounded wait that gave
+// up) go to the status word, which kvfx_device_status reads with the others.
 #include <algorithm>
 #include <mutex>
 #include <string>
@@ -32,21 +40,31 @@ namespace {
 constexpr uint64_t kNoAllocScratchBytes = 16ull << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ unsigned g_noalloc_status;  // KVFX_FLAG_* bits of this entry point's launches
 
+struct DeviceState {
+    void* scratch = nullptr;    // device address of g_noalloc_scratch
+    unsigned* status = nullptr; // device address of g_noalloc_status
+    uint32_t counter_heads = 0; // KV heads the counter region was last laid out for (0: never)
+};
 std::mutex g_scratch_mu;
-void* g_scratch_ptr[64] = {nullptr};
+DeviceState g_state[64];
 
-// Device address of g_noalloc_scratch on `device` (which must be current).
-cudaError_t scratch_address(int device, void** out) {
+// Set-up of `device` (which must be current), once: the symbols' addresses.
+cudaError_t device_state(int device, DeviceState** out) {
     if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (g_scratch_ptr[device] == nullptr) {
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    DeviceState& st = g_state[device];
+    if (st.scratch == nullptr) {
+        void* scratch = nullptr;
+        void* status = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&scratch, g_noalloc_scratch);
         if (e != cudaSuccess) return e;
-        g_scratch_ptr[device] = p;
+        e = cudaGetSymbolAddress(&status, g_noalloc_status);
+        if (e != cudaSuccess) return e;
+        st.scratch = scratch;
+        st.status = static_cast<unsigned*>(status);
     }
-    *out = g_scratch_ptr[device];
+    *out = &st;
     return cudaSuccess;
 }
 
@@ -124,17 +142,25 @@ extern "C" int kvfx_decode_noalloc(const kvfx_cache* cache, const float* q, floa
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     DecodeArgs a{q, o, block_table, seq_lens, batch, max_blocks_per_seq, max_seq_len, q_heads, 0, nullptr, 0};
 
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    DeviceState* st = nullptr;
+    cudaError_t e = device_state(c.device, &st);
+    if (e != cudaSuccess) {
+        return fail(KVFX_ECUDA, std::string("kvfx_decode_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    }
+
     // Shapes of the generic kernel need no scratch at all.
     if (decode_workspace_bytes(c, batch, q_heads, max_seq_len, 0) == 0) {
-        const cudaError_t e = launch_decode(c, a, nullptr, s);
+        e = launch_decode(c, a, st->status, s);
         return e == cudaSuccess ? KVFX_OK
                                 : fail(KVFX_ECUDA, std::string("kvfx_decode_noalloc: launch: ") + cudaGetErrorString(e));
     }
 
-    // Fewest pages per split (most parallelism) whose workspace fits the array.
+    // Fewest pages per split (most parallelism) whose workspace fits the
+    // array: the counter region (fixed by the KV heads), then the partials.
     const uint64_t pairs = batch * c.heads;
     const uint64_t per_split = 8ull * (c.hd + 2) * 4;
-    const uint64_t counters = pairs * 4;
+    const uint64_t counters = decode_counter_bytes(c.heads);
     if (counters + 256 + pairs * per_split > kNoAllocScratchBytes) {
         return fail(KVFX_ENOSPACE,
                     "kvfx_decode_noalloc: batch x num_kv_heads = " + std::to_string(pairs) +
@@ -150,21 +176,46 @@ extern "C" int kvfx_decode_noalloc(const kvfx_cache* cache, const float* q, floa
         return fail(KVFX_ENOSPACE, "kvfx_decode_noalloc: workspace of " + std::to_string(need) +
                                        " bytes exceeds the 16 MiB static scratch");
     }
-
-    void* scratch = nullptr;
-    cudaError_t e = scratch_address(c.device, &scratch);
-    if (e != cudaSuccess) {
-        return fail(KVFX_ECUDA, std::string("kvfx_decode_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-    }
-    a.workspace = scratch;
+    a.workspace = st->scratch;
     a.workspace_bytes = kNoAllocScratchBytes;
-    // The launch clears the split counters it uses on the stream (the array
-    // keeps the last call's contents).
-    CacheMaps maps;
-    if (!encode_cache_maps(c, &maps, &e)) {
-        return fail(KVFX_ECUDA, std::string("kvfx_decode_noalloc: tensor maps: ") + cudaGetErrorString(e));
+    // The counters must start at zero: they do after any launch laid out for
+    // the same number of KV heads; otherwise (first use, or the last call
+    // used another head count, whose partials may lie in this region) clear
+    // them on the stream.
+    if (st->counter_heads != c.heads) {
+        e = cudaMemsetAsync(st->scratch, 0, counters, s);
+        if (e != cudaSuccess) {
+            return fail(KVFX_ECUDA, std::string("kvfx_decode_noalloc: clear counters: ") + cudaGetErrorString(e));
+        }
+        st->counter_heads = c.heads;
     }
-    e = launch_decode_with_maps(c, a, maps, nullptr, s);
+    const CacheMaps* maps = cache_maps(c, &e);
+    if (maps == nullptr) {
+        return fail(KVFX_ECUDA, std::string("kvfx_decode_noalloc: tensor maps: ") +
+                                    cudaGetErrorString(e != cudaSuccess ? e : cudaErrorInvalidValue));
+    }
+    e = launch_decode_with_maps(c, a, *maps, st->status, s);
     return e == cudaSuccess ? KVFX_OK
                             : fail(KVFX_ECUDA, std::string("kvfx_decode_noalloc: launch: ") + cudaGetErrorString(e));
 }
+
+namespace kvfx {
+
+bool noalloc_status(int device, unsigned* flags, bool clear) {
+    *flags = 0;
+    if (device < 0 || device >= 64) return true;
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (g_state[device].status == nullptr) return true;  // never set up: nothing raised
+    int prev = 0;
+    if (cudaGetDevice(&prev) != cudaSuccess) return false;
+    if (prev != device && cudaSetDevice(device) != cudaSuccess) return false;
+    bool ok = cudaMemcpyFromSymbol(flags, g_noalloc_status, sizeof(unsigned)) == cudaSuccess;
+    if (ok && clear && *flags != 0) {
+        const unsigned zero = 0;
+        ok = cudaMemcpyToSymbol(g_noalloc_status, &zero, sizeof(unsigned)) == cudaSuccess;
+    }
+    if (prev != device) (void)cudaSetDevice(prev);
+    return ok;
+}
+
+}  // namespace kvfx

@@ -86,6 +86,15 @@ struct DecodeArgs {
     const uint64_t* new_slots = nullptr;
     uint64_t* table_out = nullptr;
 };
+// Decode workspace layout: the split counters first, then the split
+// partials. The counters (16 bits each, one per (row, KV head) of the largest
+// batch a launch takes) fill a region whose size depends only on the cache's
+// KV heads, so a workspace zero-filled once stays usable for every batch and
+// length: the launch that completes a counter's count resets it to zero.
+constexpr uint64_t kDecodeCounterRows = 65536;
+constexpr uint64_t decode_counter_bytes(uint32_t heads) {
+    return (kDecodeCounterRows * heads * 2 + 255) & ~uint64_t(255);
+}
 uint64_t decode_workspace_bytes(const CacheView& c, uint64_t batch, uint32_t q_heads,
                                 uint64_t max_len, uint32_t pages_per_split);
 uint32_t decode_pages_per_split(const CacheView& c, uint64_t batch, uint32_t q_heads,
@@ -135,8 +144,6 @@ struct CacheMaps {
     bool valid;
 };
 const CacheMaps* cache_maps(const CacheView& c, cudaError_t* err);
-// Encodes the maps into caller storage (no caching, no heap allocation).
-bool encode_cache_maps(const CacheView& c, CacheMaps* out, cudaError_t* err);
 
 // The batch-decode fast path with caller-provided tensor maps (16-bit caches,
 // head_size 64/128, block 16, group <= 8 only).
@@ -145,6 +152,10 @@ cudaError_t launch_decode_with_maps(const CacheView& c, const DecodeArgs& a, con
 // Runs the bounded-wait self-test kernel and waits for it; completed[w] = 1 if
 // warp w's wait completed, 0 if it gave up (the expected outcome).
 cudaError_t launch_wait_selftest(unsigned* status, cudaStream_t s, int* completed);
+
+// Flags raised by kvfx_decode_noalloc's launches on `device` (its own status
+// word, a device variable); cleared when `clear`. False on a CUDA error.
+bool noalloc_status(int device, unsigned* flags, bool clear);
 
 // Records the calling thread's message for kvfx_last_error().
 void set_last_error(const char* msg);

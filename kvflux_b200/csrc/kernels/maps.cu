@@ -5,6 +5,7 @@
 // {64, 16, 1, 1} elements and the 128-byte swizzle (64 16-bit elements = one
 // 128-byte swizzle span). Maps are encoded once per cache and kept for the
 // life of the process (a few hundred bytes each).
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -84,27 +85,18 @@ const CacheMaps* cache_maps(const CacheView& c, cudaError_t* err) {
     return m;
 }
 
-bool encode_cache_maps(const CacheView& c, CacheMaps* out, cudaError_t* err) {
-    *err = cudaSuccess;
-    EncodeTiled fn = encoder(err);
-    if (fn == nullptr) return false;
-    out->valid = encode_one(fn, &out->k, c.k, c) && encode_one(fn, &out->v, c.v, c);
-    if (!out->valid) *err = cudaErrorInvalidValue;
-    return out->valid;
-}
-
 int device_sm_count(int device) {
-    static int counts[64] = {0};
+    static std::atomic<int> counts[64];  // zero-initialised (static storage)
     if (device < 0 || device >= 64) return 148;
-    if (counts[device] == 0) {
-        int n = 0;
+    int n = counts[device].load(std::memory_order_relaxed);
+    if (n == 0) {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0) {
             (void)cudaGetLastError();
             n = 148;
         }
-        counts[device] = n;
+        counts[device].store(n, std::memory_order_relaxed);
     }
-    return counts[device];
+    return n;
 }
 
 }  // namespace kvfx

@@ -236,6 +236,34 @@ def test_decode_split_k_merge(pps):
     assert float(np.abs(out.cpu().numpy() - exp).max()) < TOL["bfloat16"]
 
 
+def test_decode_workspace_serves_changing_shapes_without_clearing():
+    """One workspace, zero-filled once, through launches whose batch, lengths
+    and split sizes change (so each launch's partials cover bytes that other
+    launches' layouts never use as counters only if the counters sit apart):
+    every launch matches the oracle, and the counters it used end at zero."""
+    lens_all = [5000, 33, 4097, 777, 1, 2500, 16, 9000, 300, 4100, 64, 1999]
+    c, table, lens_np, q, qh = _decode_case("bfloat16", 128, 16, 4, 4, lens_all, seed=13)
+    big = kv.lib.kvfx_decode_workspace_bytes(ctypes.byref(c.desc), len(lens_all), qh, int(lens_np.max()), 4)
+    ws = torch.zeros(int(big), dtype=torch.uint8, device="cuda")
+    hd = 128
+    for rows, pps in [(list(range(12)), 4), ([0, 2], 8), (list(range(12)), 64), ([7, 9, 0, 3, 5], 4),
+                      (list(range(12)), 0), ([1], 0), (list(range(12)), 4)]:
+        t = table[rows]
+        ln = lens_np[rows]
+        qq = q.reshape(len(lens_all), -1)[rows].reshape(-1).copy()
+        qd = torch.from_numpy(qq).cuda()
+        out = torch.full((len(rows) * qh * hd,), float("nan"), device="cuda")
+        call(kv.lib.kvfx_decode, ctypes.byref(c.desc), qd.data_ptr(), out.data_ptr(), u64(t), u64(ln), len(rows),
+             t.shape[1], qh, int(ln.max()), pps, ws.data_ptr(), ws.numel(), None)
+        exp = oracle.decode_batch(c.host_k, c.host_v, 1, c.nb, 4, 16, hd, t, ln, qh, qq, threads=8)
+        got = out.cpu().numpy()
+        assert np.isfinite(got).all(), (rows, pps)
+        assert float(np.abs(got - exp).max()) < TOL["bfloat16"], (rows, pps)
+        counters = ws[:65536 * 4 * 2].view(torch.int32)
+        assert int(counters.abs().sum()) == 0, (rows, pps)
+    assert kv.device_status(0) == 0
+
+
 @pytest.mark.parametrize("dtype,pps", [("bfloat16", 8), ("bfloat16", 0), ("float16", 64)])
 def test_decode_rescale_path(dtype, pps):
     """Q scaled by 8 (scores with ~8x the spread): running maxima rise by more

@@ -246,9 +246,9 @@ def test_config3_api_waits_for_callers_upload(cuda):
 
 def test_api_workspace_reused_across_shapes(cuda):
     """Two paged_attention_batch calls on one storage: 16 rows of 4096 tokens
-    (every (request, head, split) partial written), then 3 of those rows. The
-    second call's split counters lie where the first call's partials are: it
-    is right only if each launch starts from cleared counters."""
+    (every (request, head, split) partial written), then 3 of those rows, on
+    the storage's one workspace: right only if the first launch left every
+    split counter at zero for the second."""
     cfg = dict(batch=16, q_heads=32, kv_heads=8, head_size=128, block_size=16, min_len=4096, max_len=4096,
                dtype="bfloat16", seed=0xC0F6)
     wl = bench.Decode(kv, w, cfg, 0, 1)

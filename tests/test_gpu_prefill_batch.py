@@ -70,7 +70,7 @@ def test_batch_bit_identical_to_single_calls(dtype, kvh, group, lq, lens):
         outs.append(torch.full((max(a, 1) * qh * hd,), 777.0, device="cuda"))
         singles.append(torch.full_like(outs[-1], 555.0))
     need = max(kv.lib.kvfx_attention_workspace_bytes(ctypes.byref(c.desc), a, L, qh) for a, L in zip(lq, lens))
-    ws = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(max(need, 1), dtype=torch.uint8, device="cuda")
     _run_batch(c, table, qs, outs, lq, lens, qh, ws)
     for i, (a, L) in enumerate(zip(lq, lens)):
         if a == 0:
