@@ -22,6 +22,15 @@ __device__ __forceinline__ void raise_flag(unsigned* status, unsigned bit) {
     if (status != nullptr) atomicOr(status, bit);
 }
 
+// Programmatic dependent launch. A kernel launched with the programmatic
+// stream-serialization attribute may be scheduled before the kernel ahead of
+// it on the stream has finished; pdl_wait() then blocks until that kernel has
+// completed and its memory writes are visible (a no-op for a kernel launched
+// without the attribute), so it must precede the first global memory access.
+// pdl_allow_next() lets the stream's next such kernel be scheduled early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_allow_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

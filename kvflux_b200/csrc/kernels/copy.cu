@@ -9,6 +9,7 @@
 //   gather out[t][h][d] = K[(blocks[t / bs] * H + h) * bs + t % bs][d]
 //          (KVFlux src/v2/paged_kv_read.cu:77-85)
 #include <algorithm>
+#include <utility>
 
 #include "common.cuh"
 #include "launch.h"
@@ -33,6 +34,8 @@ __global__ void __launch_bounds__(256) write_kernel(
     const uint64_t* __restrict__ slots, typename Vec<VB>::T* __restrict__ k_cache,
     typename Vec<VB>::T* __restrict__ v_cache, Idx total, Idx heads, Idx vpr, Idx bs,
     uint64_t slot_count, unsigned* status) {
+    pdl_allow_next();
+    pdl_wait();  // launched as a dependent: the previous kernel's writes first
     const Idx stride = static_cast<Idx>(gridDim.x) * blockDim.x;
     for (Idx i = static_cast<Idx>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
         const Idx row = i / vpr;
@@ -56,6 +59,26 @@ __global__ void __launch_bounds__(256) write_kernel(
     }
 }
 
+// Launches `kernel` as a programmatic dependent of the stream's previous
+// kernel: its CTAs may be scheduled while that kernel drains (the kernel
+// waits for it with pdl_wait before touching memory). Short write launches
+// that follow one another - a serving loop's steps, a graph of them - then
+// lose the launch gap between them.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 template <int VB>
 cudaError_t write_vb(const CacheView& c, const void* k_new, const void* v_new, const uint64_t* slots,
                      uint64_t n, unsigned* status, cudaStream_t s) {
@@ -65,16 +88,16 @@ cudaError_t write_vb(const CacheView& c, const void* k_new, const void* v_new, c
     const uint64_t want = ceil_div(total, 256);
     const uint32_t grid = static_cast<uint32_t>(std::min<uint64_t>(want, 148ull * 64));
     if (total < (1ull << 31)) {
-        write_kernel<VB, uint32_t><<<grid, 256, 0, s>>>(
-            static_cast<const V*>(k_new), static_cast<const V*>(v_new), slots, reinterpret_cast<V*>(c.k),
-            reinterpret_cast<V*>(c.v), static_cast<uint32_t>(total), c.heads,
-            static_cast<uint32_t>(vpr), c.bs, c.slot_count, status);
-    } else {
-        write_kernel<VB, uint64_t><<<grid, 256, 0, s>>>(
-            static_cast<const V*>(k_new), static_cast<const V*>(v_new), slots, reinterpret_cast<V*>(c.k),
-            reinterpret_cast<V*>(c.v), total, c.heads, vpr, c.bs, c.slot_count, status);
+        return launch_dependent(write_kernel<VB, uint32_t>, dim3(grid), dim3(256), s, static_cast<const V*>(k_new),
+                                static_cast<const V*>(v_new), slots, reinterpret_cast<V*>(c.k),
+                                reinterpret_cast<V*>(c.v), static_cast<uint32_t>(total),
+                                static_cast<uint32_t>(c.heads), static_cast<uint32_t>(vpr),
+                                static_cast<uint32_t>(c.bs), c.slot_count, status);
     }
-    return cudaGetLastError();
+    return launch_dependent(write_kernel<VB, uint64_t>, dim3(grid), dim3(256), s, static_cast<const V*>(k_new),
+                            static_cast<const V*>(v_new), slots, reinterpret_cast<V*>(c.k), reinterpret_cast<V*>(c.v),
+                            total, static_cast<uint64_t>(c.heads), vpr, static_cast<uint64_t>(c.bs), c.slot_count,
+                            status);
 }
 
 // -------------------------------------------------------------- page copy ---
@@ -303,6 +326,8 @@ __global__ void __launch_bounds__(256) write_layers_kernel(
     const __grid_constant__ LayerBases bases, const uint4* __restrict__ k_new, const uint4* __restrict__ v_new,
     uint64_t layer_stride_vecs, const uint64_t* __restrict__ slots, uint32_t total, uint32_t heads, uint32_t vpr,
     uint32_t bs, uint64_t slot_count, unsigned* status) {
+    pdl_allow_next();
+    pdl_wait();  // launched as a dependent: the previous kernel's writes first
     const uint32_t layer = blockIdx.y;
     const uint4* kn = k_new + layer * layer_stride_vecs;
     const uint4* vn = v_new + layer * layer_stride_vecs;
@@ -448,10 +473,11 @@ cudaError_t launch_write_layers(const CacheView* layers, uint32_t num_layers, co
     }
     const uint32_t gx = static_cast<uint32_t>(std::max<uint64_t>(
         1, std::min<uint64_t>(ceil_div(total, 256 * kWriteLayersPer), ceil_div(148ull * 16, num_layers))));
-    write_layers_kernel<<<dim3(gx, num_layers), 256, 0, s>>>(
-        bases, static_cast<const uint4*>(k_new), static_cast<const uint4*>(v_new), layer_stride / 16, slots,
-        static_cast<uint32_t>(total), c.heads, static_cast<uint32_t>(c.row_bytes / 16), c.bs, c.slot_count, status);
-    return cudaGetLastError();
+    return launch_dependent(write_layers_kernel, dim3(gx, num_layers), dim3(256), s, bases,
+                            static_cast<const uint4*>(k_new), static_cast<const uint4*>(v_new), layer_stride / 16,
+                            slots, static_cast<uint32_t>(total), static_cast<uint32_t>(c.heads),
+                            static_cast<uint32_t>(c.row_bytes / 16), static_cast<uint32_t>(c.bs), c.slot_count,
+                            status);
 }
 
 cudaError_t launch_gather_layers(const CacheView* layers, uint32_t num_layers, const GatherArgs& a,
