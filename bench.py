@@ -606,7 +606,7 @@ def graph_ms(launch, ranks: Ranks, launches: int = 50, reps: int = 5) -> float:
 
 
 def layer_batches(kv, w, rank: int, world: int, ranks: Ranks, layers: int = 32, steps: int = 50, warmup: int = 5,
-                  graph: bool = True) -> dict:
+                  graph: bool = True, tokens: int = 1024) -> dict:
     """Config 2's step across a model's layers (Llama-3-8B: 32 layers, 8 KV
     heads x 128, bf16), one PagedKVStorage per layer on one odd/even
     fragmented pool of 8192 pages: 64 sequences of 1024 tokens. Write: the
@@ -617,17 +617,20 @@ def layer_batches(kv, w, rank: int, world: int, ranks: Ranks, layers: int = 32, 
     values (the tests check the bytes). Successive write launches rotate over
     `rot` slot sets (each sequence's last 4 positions, the 4 before them, ...)
     and as many input buffers, so that one rotation touches more bytes than
-    the 126 MB L2 holds and every launch reads and writes HBM."""
+    the 126 MB L2 holds and every launch reads and writes HBM. `tokens`
+    shortens the sequences (and the pool with them) for profiling runs: the
+    write's bytes do not depend on it."""
     import torch
 
     heads, hd, bs = 8 // world, 128, 16
-    nseq, total, new = 64, 1024, 4
-    b = w.decode_batch_on_pool(8192, bs, [total] * nseq, seed=0xC0F2 + rank, mode="odd")
+    nseq, total, new = 64, tokens, 4
+    pool_pages = 8192 if tokens == 1024 else 2 * nseq * (-(-tokens // bs)) + 2
+    b = w.decode_batch_on_pool(pool_pages, bs, [total] * nseq, seed=0xC0F2 + rank, mode="odd")
     dev = torch.cuda.current_device()
     stores = [kv.PagedKVStorage(b.pool, heads, hd, kv.DType.BFloat16, dev) for _ in range(layers)]
     arr = (kv.KvfxCache * layers)(*[kv.cache_descriptor(st) for st in stores])
     row = heads * hd * 2
-    rot = max(2, -(-2 * 126_000_000 // max(1, layers * nseq * new * row * 2 * 2)))
+    rot = min(total // new, max(2, -(-2 * 126_000_000 // max(1, layers * nseq * new * row * 2 * 2))))
     slot_sets = [np.array(kv.build_slot_mapping([(s, p) for s in b.sequences
                                                  for p in range(total - new * (r + 1), total - new * r)]), np.uint64)
                  for r in range(rot)]
@@ -673,7 +676,7 @@ def layer_batches(kv, w, rank: int, world: int, ranks: Ranks, layers: int = 32, 
     w_bytes = ranks.reduce(float(layers * (n * row * 2 * 2 + n * 8)), "sum")
     g_bytes = ranks.reduce(float(layers * nseq * total * row * 2 * 2 + table.nbytes), "sum")
     out = {"workload": f"{layers} layers x config2 shapes (8 KV heads x 128 bf16), one storage per layer on one "
-                       f"8192-page odd/even pool, 64 sequences x 1024 tokens",
+                       f"{pool_pages}-page odd/even pool, 64 sequences x {total} tokens",
            "write_tokens": n, "write_rotation": f"{rot} slot/input sets, {rot * w_bytes / world / 1e6:.0f} MB "
                                                  f"touched per rotation (L2 126 MB)",
            "write_ms_per_launch": w_ms, "write_layer_tokens_per_s": layers * n / (w_ms * 1e-3),
@@ -968,7 +971,7 @@ def only_case(args, ranks: Ranks, kv, w, peak: float) -> int:
         out.update({"case": args.only, "batch": cfg["batch"], "gbs": out["fused_kv_gbs"]})
     elif args.only == "layers":
         out = layer_batches(kv, w, ranks.rank, ranks.world, ranks, layers=args.batch or 32, steps=args.steps,
-                            warmup=args.warmup, graph=args.steps >= 10)
+                            warmup=args.warmup, graph=args.steps >= 10, tokens=args.tokens or 1024)
         out.update({"case": args.only, "gbs": out["gather_gbs"]})
     elif args.only == "prefill4":
         pf = Prefill(kv, w, w.CONFIG4)
@@ -1014,6 +1017,8 @@ def main(argv=None) -> int:
     ap.add_argument("--batch", type=int, default=None, help="override the batch: decode requests, write/gather sequences (profiling runs)")
     ap.add_argument("--shard", type=int, default=None,
                     help="with --only decode5/decode3 on one GPU: time rank 0's shard of an N-way KV-head split")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="with --only layers: tokens per sequence (the pool shrinks with it; profiling runs)")
     ap.add_argument("--pps", type=int, default=None,
                     help="with --only decode5/decode3: pages per split instead of the library's choice")
     args = ap.parse_args(argv)

@@ -109,6 +109,12 @@ decode_mma_kernel(const __grid_constant__ DecodeParams p, const __grid_constant_
     const uint32_t split = blockIdx.x, kh = blockIdx.y;
     const uint64_t r = blockIdx.z;
 
+    // Launched as a programmatic dependent: the stream's next kernel may be
+    // scheduled as soon as every CTA of this one has started (so its CTAs
+    // take the SMs this launch's last wave leaves), and this one reads
+    // nothing before the kernel ahead of it has completed.
+    pdl_allow_next();
+    pdl_wait();
     const uint64_t len = p.lens != nullptr ? p.lens[r] : p.single_len;
     const uint64_t npages = ceil_div(len, 16);
     const uint32_t nsplits = static_cast<uint32_t>(ceil_div(npages, p.pages_per_split));
@@ -506,9 +512,17 @@ cudaError_t launch_fast(const CacheView& c, const DecodeArgs& a, const CacheMaps
     p.table_out = a.table_out;
     p.k_base = c.k;
     p.v_base = c.v;
-    dim3 grid(max_splits, c.heads, static_cast<uint32_t>(a.batch));
-    decode_mma_kernel<HD, T><<<grid, kWarps * 32, Sh::kSmem, s>>>(p, maps->k, maps->v);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(max_splits, c.heads, static_cast<uint32_t>(a.batch));
+    cfg.blockDim = dim3(kWarps * 32);
+    cfg.dynamicSmemBytes = Sh::kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, decode_mma_kernel<HD, T>, p, maps->k, maps->v);
 }
 
 uint32_t clamp_pps(const CacheView& c, uint64_t max_len, uint32_t pps) {
