@@ -530,6 +530,23 @@ class WriteGather:
                                                     self.lens.data_ptr(), self.nseq, self.width, self.pk.data_ptr(),
                                                     self.pv.data_ptr(), stream), "kvfx_gather_batch")
 
+    def gather_one_by_one(self, stream, tma: bool):
+        """Every sequence gathered by its own call: kvfx_gather (the
+        single-sequence entry point read_paged_kv uses: TMA tensor copies) or
+        kvfx_gather_batch over that one row (the 16-byte load/store kernel)."""
+        per = self.total_len * self.heads * self.hd * 2
+        for r in range(self.nseq):
+            if tma:
+                self.kv.check(self.kv.lib.kvfx_gather(ctypes.byref(self.desc), self.table.data_ptr() + r * self.width * 8,
+                                                      self.total_len, self.k_out.data_ptr() + r * per,
+                                                      self.v_out.data_ptr() + r * per, stream), "kvfx_gather")
+            else:
+                self.kv.check(self.kv.lib.kvfx_gather_batch(ctypes.byref(self.desc),
+                                                            self.table.data_ptr() + r * self.width * 8,
+                                                            self.lens.data_ptr() + r * 8, 1, self.width,
+                                                            self.pk.data_ptr() + r * 8, self.pv.data_ptr() + r * 8,
+                                                            stream), "kvfx_gather_batch")
+
     def graph_write_ms(self, launches: int = 100) -> float:
         """Per-launch time of `launches` back-to-back writes captured in a CUDA graph."""
         import torch
@@ -982,7 +999,7 @@ def only_case(args, ranks: Ranks, kv, w, peak: float) -> int:
                "per_sequence_calls_ms_per_step": total1 / args.steps,
                "tflops": pf.flops / (ms * 1e-3) / 1e12, "gbs": 0.0}
         out["frac_of_bf16_peak"] = out["tflops"] / load_bf16_peak()[0]
-    else:
+    elif args.only in ("write", "gather"):
         cfg = dict(w.CONFIG2)
         if args.batch:  # fewer sequences on a proportionally smaller pool
             cfg["pool_pages"] = max(1, cfg["pool_pages"] * args.batch // cfg["sequences"])
@@ -994,6 +1011,17 @@ def only_case(args, ranks: Ranks, kv, w, peak: float) -> int:
         nbytes = wg.write_bytes if args.only == "write" else wg.gather_bytes
         out = {"case": args.only, "ms_per_launch": ms, "algorithmic_bytes": nbytes,
                "gbs": nbytes / (ms * 1e-3) / 1e9}
+    else:  # gather_tma, gather_ldst
+        cfg = dict(w.CONFIG2)
+        if args.batch:  # fewer sequences on a proportionally smaller pool
+            cfg["pool_pages"] = max(1, cfg["pool_pages"] * args.batch // cfg["sequences"])
+            cfg["sequences"] = args.batch
+        wg = WriteGather(kv, w, cfg, ranks.rank, ranks.world)
+        tma = args.only == "gather_tma"
+        per, total = time_launches(lambda st: wg.gather_one_by_one(st, tma), args.steps, args.warmup, ranks)
+        ms = total / args.steps
+        out = {"case": args.only, "ms_per_step": ms, "sequences": wg.nseq, "algorithmic_bytes": wg.gather_bytes,
+               "gbs": wg.gather_bytes / (ms * 1e-3) / 1e9}
     out["frac_of_peak"] = out["gbs"] / peak
     torch.cuda.synchronize()
     if ranks.rank == 0:
@@ -1012,7 +1040,8 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="headline decode only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather", "prefill4", "step5", "layers"],
+    ap.add_argument("--only", choices=["decode5", "decode3", "write", "gather", "gather_tma", "gather_ldst",
+                                       "prefill4", "step5", "layers"],
                     help="run one kernel's case alone (profiling runs); prints a short JSON line")
     ap.add_argument("--batch", type=int, default=None, help="override the batch: decode requests, write/gather sequences (profiling runs)")
     ap.add_argument("--shard", type=int, default=None,

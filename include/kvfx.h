@@ -77,7 +77,10 @@ int kvfx_write(const kvfx_cache* cache, const void* k_new, const void* v_new,
 /*
  * Gather of one sequence: k_out[t][h][:] = K[blocks[t / bs]][h][t % bs][:] for
  * t < num_tokens (V alike). blocks: device uint64[ceil(num_tokens / bs)].
- * Outputs must not overlap each other or the cache.
+ * Outputs must not overlap each other or the cache. Rows that are 16-byte
+ * multiples of at most 256 elements, with 16-byte aligned bases, move by TMA
+ * tensor copies (one load and one store per page and KV head); other shapes
+ * by vector loads and stores.
  * Replaces the kernel launch of read_paged_kv (KVFlux src/v2/paged_kv_read.cu:90-102).
  */
 int kvfx_gather(const kvfx_cache* cache, const uint64_t* blocks, uint64_t num_tokens,

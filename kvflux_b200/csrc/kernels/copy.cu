@@ -9,6 +9,7 @@
 //   gather out[t][h][d] = K[(blocks[t / bs] * H + h) * bs + t % bs][d]
 //          (KVFlux src/v2/paged_kv_read.cu:77-85)
 #include <algorithm>
+#include <atomic>
 #include <utility>
 
 #include "common.cuh"
@@ -516,6 +517,141 @@ cudaError_t launch_copy_page(const CacheView& c, uint64_t src, uint64_t dst, uns
     }
 }
 
+// ------------------------------------------------------------- gather (TMA) ---
+// One sequence gathered by the tensor memory accelerator. Unit = (page, KV
+// head): its K and V tiles (block_size rows of head_size elements, one
+// contiguous run in the cache) are loaded with one 4-D tensor copy each into
+// shared memory and stored with one 3-D tensor copy each through maps over
+// the outputs [tokens][heads][head_size] whose box is {head_size, 1 head,
+// block_size tokens}: the box walks the heads' stride in global memory, so
+// the page's [head][token] order becomes the output's [token][head] order
+// with no work in shared memory. A store past the sequence's last token is
+// clipped by the copy engine. One warp per CTA, one lane issuing: a ring of
+// kGatherTmaSlots units; a slot is refilled once the stores that read it
+// have finished reading (bulk-group waits). Tiles sit at 128-byte aligned
+// shared-memory offsets (tile_stride), as tensor copies require.
+constexpr int kGatherTmaSlots = 4;
+
+__global__ void __launch_bounds__(32) gather_tma_kernel(
+    const __grid_constant__ CUtensorMap in_k, const __grid_constant__ CUtensorMap in_v,
+    const __grid_constant__ CUtensorMap out_k, const __grid_constant__ CUtensorMap out_v,
+    const uint64_t* __restrict__ blocks, uint64_t num_tokens, uint32_t heads, uint32_t bs, uint32_t tile_bytes,
+    uint32_t tile_stride, uint64_t num_blocks, unsigned* status) {
+    extern __shared__ unsigned char smem_raw[];
+    __shared__ uint64_t full[kGatherTmaSlots];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                           ~uintptr_t(1023));
+    pdl_allow_next();
+    if (!elect_one()) return;
+    pdl_wait();  // launched as a dependent: the previous kernel's writes first
+    const uint64_t pages = ceil_div(num_tokens, bs);
+    const uint64_t units = pages * heads;
+    const uint64_t first = blockIdx.x;
+    const uint64_t n_my = first < units ? ceil_div(units - first, gridDim.x) : 0;
+    for (int i = 0; i < kGatherTmaSlots; ++i) mbar_init(&full[i], 1);
+    fence_mbarrier_init();
+    prefetch_tensormap(&in_k);
+    prefetch_tensormap(&in_v);
+    prefetch_tensormap(&out_k);
+    prefetch_tensormap(&out_v);
+    bool skip[kGatherTmaSlots] = {};
+    auto load = [&](uint64_t k) {  // unit k of this CTA into slot k % kGatherTmaSlots
+        if (k >= n_my) return;
+        const int st = static_cast<int>(k % kGatherTmaSlots);
+        const uint64_t u = first + k * gridDim.x;
+        const uint64_t page = u / heads;
+        const uint32_t h = static_cast<uint32_t>(u - page * heads);
+        const uint64_t blk = __ldg(blocks + page);
+        skip[st] = blk >= num_blocks;
+        if (skip[st]) {  // never followed: flagged, the output rows stay as they were
+            raise_flag(status, KVFX_FLAG_BAD_INDEX);
+            mbar_arrive(&full[st]);
+            return;
+        }
+        unsigned char* dst = smem + st * 2 * tile_stride;
+        mbar_arrive_expect_tx(&full[st], 2 * tile_bytes);
+        tma_load_4d(dst, &in_k, 0, 0, static_cast<int>(h), static_cast<int>(blk), &full[st]);
+        tma_load_4d(dst + tile_stride, &in_v, 0, 0, static_cast<int>(h), static_cast<int>(blk), &full[st]);
+    };
+    for (uint64_t k = 0; k + 1 < kGatherTmaSlots; ++k) load(k);
+    uint64_t waited = 0;  // units whose loads this lane has seen complete
+    for (uint64_t k = 0; k < n_my; ++k) {
+        const int st = static_cast<int>(k % kGatherTmaSlots);
+        if (!mbar_wait(&full[st], static_cast<uint32_t>(k / kGatherTmaSlots) & 1u, status)) break;
+        waited = k + 1;
+        if (!skip[st]) {
+            fence_proxy_async_smem();
+            const uint64_t u = first + k * gridDim.x;
+            const uint64_t page = u / heads;
+            const int h = static_cast<int>(u - page * heads);
+            const int t0 = static_cast<int>(page * bs);
+            const unsigned char* src = smem + st * 2 * tile_stride;
+            tma_store_3d(&out_k, 0, h, t0, src);
+            tma_store_3d(&out_v, 0, h, t0, src + tile_stride);
+        }
+        bulk_commit();
+        bulk_wait_read<1>();  // unit k - 1's stores have read their slot
+        load(k + kGatherTmaSlots - 1);
+    }
+    // Loads issued but not waited for (a wait gave up): let them land
+    // (bounded) before the shared memory is released.
+    const uint64_t issued = n_my < waited + kGatherTmaSlots - 1 ? n_my : waited + kGatherTmaSlots - 1;
+    for (uint64_t k = waited; k < issued; ++k) {
+        (void)mbar_wait(&full[k % kGatherTmaSlots], static_cast<uint32_t>(k / kGatherTmaSlots) & 1u, status);
+    }
+    bulk_wait<0>();
+}
+
+// One sequence through gather_tma_kernel, when its rows are whole 16-byte
+// multiples of at most 256 elements, its tiles fit the ring (<= 8 KiB per
+// tile) and every base is 16-byte aligned; false (nothing launched) otherwise.
+bool gather_tma(const CacheView& c, const GatherArgs& a, unsigned* status, cudaStream_t s, cudaError_t* err) {
+    *err = cudaSuccess;
+    const uint64_t tile = static_cast<uint64_t>(c.bs) * c.row_bytes;
+    if (c.row_bytes % 16 != 0 || c.hd > 256 || c.bs > 256 || tile > 8192 || a.single_len >= (1ull << 31) ||
+        c.num_blocks >= (1ull << 31) || c.heads >= (1u << 31) || ((reinterpret_cast<uintptr_t>(c.k) |
+        reinterpret_cast<uintptr_t>(c.v) | reinterpret_cast<uintptr_t>(a.k_out) |
+        reinterpret_cast<uintptr_t>(a.v_out)) & 15u) != 0 || ceil_div(a.single_len, c.bs) > a.max_blocks) {
+        return false;
+    }
+    const CacheMaps* in = gather_maps(c, err);
+    if (in == nullptr) return false;
+    const CUtensorMapDataType t = c.elem == 4 ? CU_TENSOR_MAP_DATA_TYPE_UINT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+    const uint64_t dims[3] = {c.hd, c.heads, a.single_len};
+    const uint64_t strides[2] = {c.row_bytes, c.row_bytes * c.heads};
+    const uint32_t box[3] = {c.hd, 1, c.bs};
+    CUtensorMap out_k, out_v;
+    if (!encode_tiled(&out_k, t, 3, a.k_out, dims, strides, box, err) ||
+        !encode_tiled(&out_v, t, 3, a.v_out, dims, strides, box, err)) {
+        return false;
+    }
+    const uint64_t tile_stride = (tile + 127) & ~uint64_t(127);  // tensor copies need 128-byte aligned smem
+    const uint32_t smem = static_cast<uint32_t>(kGatherTmaSlots * 2 * tile_stride + 1024);
+    static std::atomic<int> attr_done[64];
+    if (c.device < 0 || c.device >= 64 || !attr_done[c.device].load(std::memory_order_acquire)) {
+        *err = cudaFuncSetAttribute(gather_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 65536 + 1024);
+        if (*err != cudaSuccess) return true;
+        if (c.device >= 0 && c.device < 64) attr_done[c.device].store(1, std::memory_order_release);
+    }
+    const uint64_t units = ceil_div(a.single_len, c.bs) * c.heads;
+    const uint64_t per_sm = std::max<uint64_t>(1, (227ull * 1024) / (smem + 1024));
+    const uint32_t grid = static_cast<uint32_t>(std::min<uint64_t>(units, device_sm_count(c.device) * per_sm));
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    *err = cudaLaunchKernelEx(&cfg, gather_tma_kernel, in->k, in->v, out_k, out_v, a.blocks, a.single_len, c.heads,
+                              c.bs, static_cast<uint32_t>(tile), static_cast<uint32_t>(tile_stride), c.num_blocks,
+                              status);
+    return true;
+}
+
 cudaError_t launch_gather(const CacheView& c, const GatherArgs& a, unsigned* status, cudaStream_t s) {
     if (a.batch == 0 || a.max_len == 0) return cudaSuccess;
     // Direct path: rows are whole 16-byte vectors, the caches and (for one
@@ -523,6 +659,10 @@ cudaError_t launch_gather(const CacheView& c, const GatherArgs& a, unsigned* sta
     // 31 bits. Batched outputs are only known on the device: the kernel
     // refuses a misaligned one with the bad-index flag.
     const bool single = a.k_out_list == nullptr;
+    if (single && !a.force_simt && a.out_offset == 0 && a.single_len != 0) {
+        cudaError_t e = cudaSuccess;
+        if (gather_tma(c, a, status, s, &e)) return e;
+    }
     bool direct = !a.force_simt && a.out_offset == 0 && c.row_bytes % 16 == 0 && c.page_bytes / 16 < (1ull << 31) &&
                   (reinterpret_cast<uintptr_t>(c.k) | reinterpret_cast<uintptr_t>(c.v)) % 16 == 0;
     if (direct && single) {

@@ -144,6 +144,13 @@ struct CacheMaps {
     bool valid;
 };
 const CacheMaps* cache_maps(const CacheView& c, cudaError_t* err);
+// Unswizzled maps over the K and V caches, one box = one (page, head) tile of
+// block_size rows (the TMA gather's loads; cached per cache).
+const CacheMaps* gather_maps(const CacheView& c, cudaError_t* err);
+// Encodes a tiled, unswizzled tensor map (dims and box innermost first,
+// strides in bytes for dims 1..rank-1).
+bool encode_tiled(CUtensorMap* map, CUtensorMapDataType type, uint32_t rank, void* base, const uint64_t* dims,
+                  const uint64_t* strides, const uint32_t* box, cudaError_t* err);
 
 // The batch-decode fast path with caller-provided tensor maps (16-bit caches,
 // head_size 64/128, block 16, group <= 8 only).
