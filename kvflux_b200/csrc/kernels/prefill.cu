@@ -10,21 +10,28 @@
 // Warp roles (12 warps):
 //   warp 0      K producer, warp 2 V producer: per KV tile 16 tensor loads
 //               (8 pages x 2 64-dim halves, 128-byte swizzle, no multicast)
-//               into a 3-slot K ring and a 2-slot V ring.
+//               into a 4-slot K ring and a 2-slot V ring.
 //   warp 1      owns TMEM (512 columns) and issues every tcgen05.mma from one
-//               thread: S(g) = Q K_g^T into S[g%3], then O += P(g) V_g with
-//               P read from TMEM; QK runs two tiles ahead of PV.
+//               thread: S(g) = Q K_g^T into S[g%2] with Q read from TMEM, then
+//               O += P(g) V_g with P read from TMEM; QK runs two tiles ahead
+//               of PV.
 //   warp 3      idle.
 //   warps 4-7   softmax, one query row per thread (TMEM lane = row): scores
 //               from TMEM, causal mask, online softmax in base 2, P = exp2(S-m)
 //               written back over its own S columns as packed 16-bit hi/lo
 //               pairs; at a unit's last tile, O / l from TMEM to global memory.
 //   warps 8-11  Q staging: the next unit's Q rows are loaded into registers
-//               while the current unit runs, and split into hi/lo 16-bit
-//               halves in shared memory once its last QK has completed.
-// TMEM columns: S/P buffers 0, 128, 256; O 384. S[b] holds P(g) (g%3 == b)
-// until PV(g) completes; the MMA thread waits for that completion before
-// writing S(g+3) there, while PV(g+1) keeps the tensor pipe busy.
+//               while the current unit runs, and written as hi/lo 16-bit
+//               halves into the Q columns of TMEM once its last QK has
+//               completed.
+// TMEM columns: S/P buffers 0 and 128; O 256; Q 384 (hi 384..447, lo
+// 448..511). S[g%2] holds P(g) until PV(g) has read it; QK(g+2), which
+// overwrites it, is issued after PV(g) by the same thread, and tcgen05.mma
+// operations issued by one thread execute in issue order, so PV(g) has read
+// P(g) before QK(g+2) writes there (no wait in between; the tensor pipe
+// stays busy). Q in TMEM halves the shared-memory operand traffic of QK
+// (only K is read from shared memory), the resource that bounded the
+// tile rate when both operands came from there.
 // Precision: Q (FP32 in the API) and P are each fed as two 16-bit operands,
 // hi = round(x) and lo = round(x - hi), accumulated into the same TMEM tile
 // (S = Q_hi K + Q_lo K, O += P_hi V + P_lo V): ~16 mantissa bits and FP32-class
@@ -50,25 +57,24 @@ constexpr int kBM = 128;         // query rows per unit
 constexpr int kBN = 128;         // KV tokens per tile (8 pages of 16)
 constexpr int kHD = 128;         // head size handled here
 constexpr uint32_t kMaxPrefillSeqs = KVFX_MAX_PREFILL_SEQS;  // sequences per launch
-constexpr int kKStages = 3;      // K ring depth
+constexpr int kKStages = 4;      // K ring depth
 constexpr int kVStages = 2;      // V ring depth
-constexpr int kSBufs = 3;        // S/P buffers in TMEM
+constexpr int kSBufs = 2;        // S/P buffers in TMEM
 constexpr int kThreads = 384;    // 12 warps
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemO = kSBufs * kBN;          // O accumulator column
-// The producers' waits on s_full / pv_done rely on a ring of no more slots
-// than there are S buffers (see produce()).
-static_assert(kKStages <= kSBufs && kVStages <= kSBufs, "ring deeper than the S buffers");
+constexpr uint32_t kTmemQ = kTmemO + kHD;          // Q: hi pairs, then lo pairs (64 columns each)
+static_assert(kTmemQ + kHD == kTmemCols, "TMEM budget");
+// The V producer's waits on pv_done rely on a ring of no more slots than
+// there are S buffers (see produce()); the K ring has its own free barriers.
+static_assert(kVStages <= kSBufs, "V ring deeper than the S buffers");
 
 // Shared-memory layout (byte offsets from a 1024-aligned base).
-constexpr uint32_t kQAtom = kBM * 128;             // [128 rows][64 dims] 16-bit, 16 KiB
-constexpr uint32_t kQBytes = 2 * kQAtom;           // 128 dims, 32 KiB (hi; lo follows)
 constexpr uint32_t kKVHalf = kBN * 128;            // [128 tokens][64 dims], 16 KiB
 constexpr uint32_t kKVTile = 2 * kKVHalf;          // 32 KiB
-constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kOffQ + 2 * kQBytes;
+constexpr uint32_t kOffK = 0;
 constexpr uint32_t kOffV = kOffK + kKStages * kKVTile;
-constexpr uint32_t kSmemBytes = kOffV + kVStages * kKVTile;   // 224 KiB
+constexpr uint32_t kSmemBytes = kOffV + kVStages * kKVTile;   // 192 KiB
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
 
 // One sequence of a launch: its Q and O ([q_tokens][q_heads][128] FP32), its
@@ -156,12 +162,6 @@ __device__ __forceinline__ uint64_t widen2<__half>(uint32_t h) {
     return f2_pack(__low2float(x), __high2float(x));
 }
 
-// Byte offset of 16-byte chunk `c` of row `r` in a K-major 128-byte-swizzled
-// atom of rows 128 bytes wide.
-__device__ __forceinline__ uint32_t swz_row(uint32_t r, uint32_t c) {
-    return (r >> 3) * 1024 + (r & 7) * 128 + (((c ^ r) & 7) << 4);
-}
-
 // Page id of page `lane` of KV tile j of sequence s in lanes 0..7 (one load
 // per lane, all in one memory round trip); 0 in the other lanes.
 __device__ __forceinline__ uint64_t tile_page_id(const PrefillParams& p, uint32_t s, uint32_t j, uint32_t lane) {
@@ -199,13 +199,13 @@ __device__ __forceinline__ void load_kv_tile(const PrefillParams& p, const CUten
 // Producer loop of one ring (K or V) of `kStages` slots, run by a whole warp
 // (voted waits, one elected lane issuing the copies): before tile g is
 // loaded into slot g % kStages, the MMA that read tile g - kStages must have
-// completed, which the MMA warp's commit to done[(g - kStages) % kSBufs]
-// signals (s_full for K: QK(g) completes; pv_done for V: PV(g) completes).
-// Neither barrier can run a phase ahead: tile g's own MMA needs this load.
-// The next tile's page ids are fetched while waiting for its slot. At the
-// end, waits for its own copies in flight.
+// completed, which done[(g - kStages) % nDone] signals (K: k_free, one per
+// slot, arrived once QK(g) completes; V: pv_done, the MMA warp's commit once
+// PV(g) completes, one per S buffer). Neither barrier can run a phase ahead:
+// tile g's own MMA needs this load. The next tile's page ids are fetched
+// while waiting for its slot. At the end, waits for its own copies in flight.
 __device__ __noinline__ void produce(const PrefillParams& p, const CUtensorMap* map, unsigned char* ring,
-                                     uint64_t* full, uint64_t* done, uint32_t kStages) {
+                                     uint64_t* full, uint64_t* done, uint32_t kStages, uint32_t nDone) {
     const uint32_t lane = threadIdx.x & 31u;
     const bool leader = elect_one();
     auto wait = [&](uint64_t* bar, uint32_t phase) {
@@ -220,7 +220,7 @@ __device__ __noinline__ void produce(const PrefillParams& p, const CUtensorMap* 
         const uint32_t g = c.g, st = g % kStages;
         if (g >= kStages) {
             const uint32_t prev = g - kStages;
-            if (!wait(&done[prev % kSBufs], (prev / kSBufs) & 1u)) break;
+            if (!wait(&done[prev % nDone], (prev / nDone) & 1u)) break;
         }
         load_kv_tile(p, map, ring + st * kKVTile, c.u.kh, id, leader, &full[st]);
         issued = g + 1;
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap) {
     extern __shared__ unsigned char smem_raw[];
-    __shared__ uint64_t k_full[kKStages], v_full[kVStages];
+    __shared__ uint64_t k_full[kKStages], k_free[kKStages], v_full[kVStages];
     __shared__ uint64_t s_full[kSBufs], p_full[kSBufs], pv_done[kSBufs];
     __shared__ uint64_t q_full, q_free, o_full, o_free, mma_done;
     __shared__ uint32_t tmem_base_slot;
@@ -247,7 +247,10 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (tid == 0) {
-        for (int s = 0; s < kKStages; ++s) mbar_init(&k_full[s], 1);
+        for (int s = 0; s < kKStages; ++s) {
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_free[s], 1);
+        }
         for (int s = 0; s < kVStages; ++s) mbar_init(&v_full[s], 1);
         for (int b = 0; b < kSBufs; ++b) {
             mbar_init(&s_full[b], 1);
@@ -272,10 +275,10 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
 
     if (warp == 0) {
         // ---------------------------------------------------- K producer ---
-        produce(p, &kmap, smem + kOffK, k_full, s_full, kKStages);
+        produce(p, &kmap, smem + kOffK, k_full, k_free, kKStages, kKStages);
     } else if (warp == 2) {
         // ---------------------------------------------------- V producer ---
-        produce(p, &vmap, smem + kOffV, v_full, pv_done, kVStages);
+        produce(p, &vmap, smem + kOffV, v_full, pv_done, kVStages, kSBufs);
     } else if (warp == 1) {
         // ----------------------------------------------------- MMA issuer ---
         // The whole warp runs the schedule (its values stay warp-uniform);
@@ -301,23 +304,21 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
             // Operand descriptors are formed once; every MMA adds a constant
             // offset (16-byte units, the descriptor's low start-address field;
             // shared addresses stay below 2^18 so nothing carries out).
-            const uint64_t q_desc0 = tc::desc_k_major(sbase + kOffQ);
             const uint64_t k_desc0 = tc::desc_k_major(sbase + kOffK);
             const uint64_t v_desc0 = tc::desc_mn_major(sbase + kOffV, kKVHalf);
             TileCursor qk, pv;
             qk.init(p);
             pv.init(p);
-            // S(g) = Q K_g^T into S[g%3]; S[g%3] held P(g-3) until PV(g-3)
-            // completed. Each step is split into its waits, its 16 MMAs and
-            // its commits, so that the next step's waits can run while the
-            // tensor pipe still has this step's last MMAs queued.
+            // S(g) = Q K_g^T into S[g%2], which held P(g-2): PV(g-2) was
+            // issued before this step by this thread and so reads P(g-2)
+            // before these MMAs write there. Each step is split into its
+            // waits, its 16 MMAs and its commits, so that the next step's
+            // waits can run while the tensor pipe still has this step's last
+            // MMAs queued.
             auto qk_wait = [&]() -> bool {
                 const uint32_t g = qk.g;
-                if (qk.j == 0 && !wait(&q_full, qk.k & 1u)) return false;
-                if (g >= kSBufs) {
-                    if (!wait2(&k_full[g % kKStages], (g / kKStages) & 1u, &pv_done[g % kSBufs],
-                               ((g / kSBufs) - 1) & 1u))
-                        return false;
+                if (qk.j == 0) {
+                    if (!wait2(&q_full, qk.k & 1u, &k_full[g % kKStages], (g / kKStages) & 1u)) return false;
                 } else if (!wait(&k_full[g % kKStages], (g / kKStages) & 1u)) {
                     return false;
                 }
@@ -328,15 +329,16 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
                 const uint32_t g = qk.g;
                 const uint32_t d = tmem + (g % kSBufs) * kBN;
                 const uint64_t k_desc = k_desc0 + (((g % kKStages) * kKVTile) >> 4);
-                // Q_hi then Q_lo, 8 K-steps of 16 each (unrolled: the constant
-                // operand offsets fold into the descriptor adds).
+                // Q_hi then Q_lo (A from TMEM: 8 columns per 16 dims), 8
+                // K-steps of 16 each (unrolled: the constant operand offsets
+                // fold into the address and descriptor adds).
 #pragma unroll
                 for (uint32_t i = 0; i < 16; ++i) {
                     if (i < from || i >= to) continue;
                     const uint32_t part = i >> 3, kk = i & 7;
-                    const uint32_t a_off = part * kQBytes + (kk >> 2) * kQAtom + (kk & 3) * 32;
+                    const uint32_t a = tmem + kTmemQ + part * (kHD / 2) + kk * 8;
                     const uint32_t b_off = (kk >> 2) * kKVHalf + (kk & 3) * 32;
-                    if (leader) tc::mma(d, q_desc0 + (a_off >> 4), k_desc + (b_off >> 4), id_qk, i > 0 ? 1u : 0u);
+                    if (leader) tc::mma_ts(d, a, k_desc + (b_off >> 4), id_qk, i > 0 ? 1u : 0u);
                 }
             };
             auto qk_finish = [&]() {
@@ -433,6 +435,8 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
                 const uint32_t b = g % kSBufs;
                 if (!wait_all(&s_full[b], (g / kSBufs) & 1u)) { ok = false; break; }
                 tc::fence_after_sync();
+                // QK(g) has completed, so it has read K tile g: free its slot.
+                if (warp == 4 && lane == 0) mbar_arrive(&k_free[g % kKStages]);
                 const uint32_t tS = tmem + b * kBN + lane_base;
                 // Causal mask: column c is visible iff j*128 + c <= pos (pos <
                 // kv_tokens for live rows). Applied branch-free as
@@ -596,9 +600,11 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
         }
     } else if (warp >= 8) {
         // ----------------------------------------------------- Q staging ---
-        const uint32_t r = static_cast<uint32_t>(tid - 256);  // row within the unit
-        unsigned char* qhi = smem + kOffQ;
-        unsigned char* qlo = qhi + kQBytes;
+        // Warp 8 + w writes TMEM lanes 32w..32w+31 (the quarter its
+        // sub-partition may access): row r = its thread's query row.
+        const uint32_t quarter = static_cast<uint32_t>(warp & 3);
+        const uint32_t r = quarter * 32 + lane;
+        const uint32_t tQ = tmem + kTmemQ + ((quarter * 32) << 16);
         Unit u;
         for (uint32_t round = 0, k = 0; unit_at(p, round, u); ++round, ++k) {
             const uint64_t qi = u.q0 + r;
@@ -619,19 +625,22 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
 #pragma unroll
                 for (int e = 0; e < kHD; ++e) v[e] = 0.f;
             }
-            // The previous unit's last QK has read the Q tile.
-            if (k >= 1 && !mbar_wait_lean(&q_free, (k - 1) & 1u, p.status)) break;
+            // The previous unit's last QK has read the Q columns. tcgen05.st
+            // is warp-collective: the wait result is made warp-uniform.
+            if (k >= 1 && !__all_sync(0xffffffffu, mbar_wait_lean(&q_free, (k - 1) & 1u, p.status))) break;
+            tc::fence_after_sync();
+            // Column c of the hi (lo) half holds dims 2c, 2c+1 of the row.
 #pragma unroll
-            for (uint32_t cc = 0; cc < kHD / 8; ++cc) {
-                uint32_t hi[4], lo[4];
+            for (uint32_t cc = 0; cc < kHD / 16; ++cc) {
+                uint32_t hi[8], lo[8];
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    split2_fast<T>(v[8 * cc + 2 * e] * p.qscale, v[8 * cc + 2 * e + 1] * p.qscale, hi[e], lo[e]);
-                const uint32_t off = (cc >> 3) * kQAtom + swz_row(r, cc & 7);
-                *reinterpret_cast<uint4*>(qhi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4*>(qlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                for (int e = 0; e < 8; ++e)
+                    split2_fast<T>(v[16 * cc + 2 * e] * p.qscale, v[16 * cc + 2 * e + 1] * p.qscale, hi[e], lo[e]);
+                tc::st8(tQ + cc * 8, hi);
+                tc::st8(tQ + kHD / 2 + cc * 8, lo);
             }
-            fence_proxy_async_smem();
+            tc::wait_st();
+            tc::fence_before_sync();
             mbar_arrive(&q_full);
         }
     }
