@@ -19,11 +19,15 @@
 //   warps 4-7   softmax, one query row per thread (TMEM lane = row): scores
 //               from TMEM, causal mask, online softmax in base 2, P = exp2(S-m)
 //               written back over its own S columns as packed 16-bit hi/lo
-//               pairs; at a unit's last tile, O / l from TMEM to global memory.
-//   warps 8-11  Q staging: the next unit's Q rows are loaded into registers
-//               while the current unit runs, and written as hi/lo 16-bit
-//               halves into the Q columns of TMEM once its last QK has
-//               completed.
+//               pairs; at a unit's last tile, the row sums l go to shared
+//               memory and the softmax moves straight on to the next unit.
+//   warps 8-11  Q staging and epilogue: the next unit's Q rows are loaded
+//               into registers while the current unit runs, and written as
+//               hi/lo 16-bit halves into the Q columns of TMEM once its last
+//               QK has completed; then the unit's O is read from TMEM (O is
+//               released to the next unit's first PV as soon as it is in
+//               registers) and O / l is written to global memory, off the
+//               softmax's critical path.
 // TMEM columns: S/P buffers 0 and 128; O 256; Q 384 (hi 384..447, lo
 // 448..511). S[g%2] holds P(g) until PV(g) has read it; QK(g+2), which
 // overwrites it, is issued after PV(g) by the same thread, and tcgen05.mma
@@ -239,6 +243,8 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
     __shared__ uint64_t k_full[kKStages], k_free[kKStages], v_full[kVStages];
     __shared__ uint64_t s_full[kSBufs], p_full[kSBufs], pv_done[kSBufs];
     __shared__ uint64_t q_full, q_free, o_full, o_free, mma_done;
+    __shared__ uint64_t l_ready[2], l_free[2];
+    __shared__ float l_sh[2][kBM];  // row sums of a unit, by unit parity
     __shared__ uint32_t tmem_base_slot;
 
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -261,6 +267,10 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
         mbar_init(&q_free, 1);
         mbar_init(&o_full, 1);
         mbar_init(&o_free, 128);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&l_ready[b], 128);
+            mbar_init(&l_free[b], 128);
+        }
         mbar_init(&mma_done, 1);
         fence_mbarrier_init();
     }
@@ -391,11 +401,22 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
             if (ok && pv.valid) ok = pv_wait();
             // Steady state: PV(g), then QK(g + 2).
             while (ok && pv.valid) {
-                pv_mmas(0, kSplit);
                 const bool more_qk = qk.valid;
-                if (more_qk) ok = qk_wait();
-                pv_mmas(kSplit, 16);
-                pv_finish();
+                if (more_qk && qk.j == 0) {
+                    // QK(g + 2) starts a unit: its Q is staged by the warps
+                    // that also run the epilogue, after the epilogue of the
+                    // unit before the previous one, which may be waiting for
+                    // this PV's commit (when the previous unit has one tile).
+                    // So PV(g) is issued and committed before that wait.
+                    pv_mmas(0, 16);
+                    pv_finish();
+                    ok = qk_wait();
+                } else {
+                    pv_mmas(0, kSplit);
+                    if (more_qk) ok = qk_wait();
+                    pv_mmas(kSplit, 16);
+                    pv_finish();
+                }
                 if (!ok) break;
                 if (more_qk) {
                     // All of QK(g + 2) and its commit before the wait for
@@ -439,16 +460,16 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
                 if (warp == 4 && lane == 0) mbar_arrive(&k_free[g % kKStages]);
                 const uint32_t tS = tmem + b * kBN + lane_base;
                 // Causal mask: column c is visible iff j*128 + c <= pos (pos <
-                // kv_tokens for live rows). Applied branch-free as
-                // min(s, +-inf), so that NaN scores of masked columns become
-                // -inf as well; only tiles on or past the diagonal need it.
+                // kv_tokens for live rows). Applied as a select against the
+                // column's compile-time index, so that masked columns become
+                // -inf whatever they held (NaN included); only tiles on or
+                // past the diagonal need it.
                 const int64_t lim64 = pos - static_cast<int64_t>(j) * kBN;
                 const int lim = lim64 < -1 ? -1 : (lim64 > kBN ? kBN : static_cast<int>(lim64));
                 const bool masked = !__all_sync(0xffffffffu, lim >= kBN - 1);
                 auto mask32 = [&](float* v, int rel) {  // rel: lim relative to v[0]
 #pragma unroll
-                    for (int cc = 0; cc < 32; ++cc, --rel)
-                        v[cc] = fminf(v[cc], __uint_as_float(0x7F800000u | (static_cast<uint32_t>(rel) & 0x80000000u)));
+                    for (int cc = 0; cc < 32; ++cc) v[cc] = cc <= rel ? v[cc] : -INFINITY;
                 };
                 auto max32 = [](const float* v) {
                     float m[4];
@@ -463,10 +484,10 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
                     for (int e = 0; e < 4; ++e) m[e] = fmaxf(m[e], v[28 + e]);
                     return fmaxf(fmax3(m[0], m[1], m[2]), m[3]);
                 };
-                // Row maximum: all 128 scores in one TMEM round trip, or chunk
-                // by chunk with the mask on diagonal tiles.
-                float mx = -INFINITY;
-                if (!masked) {
+                // Row maximum: all 128 scores in one TMEM round trip, masked on
+                // diagonal tiles.
+                float mx;
+                {
                     float sc[kBN];
 #pragma unroll
                     for (int cb = 0; cb < kBN; cb += 32) tc::ld32(tS + cb, sc + cb);
@@ -474,16 +495,11 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
                     tc::reg_fence32(sc + 32);
                     tc::reg_fence32(sc + 64);
                     tc::reg_fence32(sc + 96);
-                    mx = fmaxf(fmaxf(max32(sc), max32(sc + 32)), fmaxf(max32(sc + 64), max32(sc + 96)));
-                } else {
-#pragma unroll 1
-                    for (int cb = 0; cb < kBN; cb += 32) {
-                        float sc[32];
-                        tc::ld32(tS + cb, sc);
-                        tc::wait_ld32(sc);
-                        mask32(sc, lim - cb);
-                        mx = fmaxf(mx, max32(sc));
+                    if (masked) {
+#pragma unroll
+                        for (int cb = 0; cb < kBN; cb += 32) mask32(sc + cb, lim - cb);
                     }
+                    mx = fmaxf(fmaxf(max32(sc), max32(sc + 32)), fmaxf(max32(sc + 64), max32(sc + 96)));
                 }
                 const bool need = mx > m_run + 8.f;  // m_run = -inf: always at a unit's first tile
                 const float m_new = need ? mx : m_run;
@@ -575,43 +591,31 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
                 mbar_arrive(&p_full[b]);
             }
             if (!ok) break;
-            // Epilogue of the unit: O / l to global memory, then O is free.
-            if (!wait_all(&o_full, k & 1u)) break;
-            tc::fence_after_sync();
-            const float inv = 1.f / l_run;
-            const uint64_t qi = u.q0 + r;
-            const bool row_live = qi < sq.q_tokens;
-            float* orow = sq.o + (qi * p.q_heads + u.qh) * kHD;
-#pragma unroll 1
-            for (int cb = 0; cb < kHD; cb += 32) {
-                float ov[32];
-                tc::ld32(tO + cb, ov);
-                tc::wait_ld32(ov);
-                if (row_live) {
-#pragma unroll
-                    for (int e = 0; e < 32; e += 4) {
-                        *reinterpret_cast<float4*>(orow + cb + e) =
-                            make_float4(ov[e] * inv, ov[e + 1] * inv, ov[e + 2] * inv, ov[e + 3] * inv);
-                    }
-                }
-            }
-            tc::fence_before_sync();
-            mbar_arrive(&o_free);
+            // Hand the unit's row sums to the epilogue warps (the buffer of
+            // this parity was last read for unit k - 2).
+            if (k >= 2 && !wait_all(&l_free[k & 1u], ((k - 2) >> 1) & 1u)) break;
+            l_sh[k & 1u][r] = l_run;
+            mbar_arrive(&l_ready[k & 1u]);
         }
     } else if (warp >= 8) {
-        // ----------------------------------------------------- Q staging ---
-        // Warp 8 + w writes TMEM lanes 32w..32w+31 (the quarter its
+        // ------------------------------------------ Q staging + epilogue ---
+        // Warp 8 + w accesses TMEM lanes 32w..32w+31 (the quarter its
         // sub-partition may access): row r = its thread's query row.
+        // tcgen05.ld/st are warp-collective: every wait result is made
+        // warp-uniform.
         const uint32_t quarter = static_cast<uint32_t>(warp & 3);
         const uint32_t r = quarter * 32 + lane;
-        const uint32_t tQ = tmem + kTmemQ + ((quarter * 32) << 16);
-        Unit u;
-        for (uint32_t round = 0, k = 0; unit_at(p, round, u); ++round, ++k) {
-            const uint64_t qi = u.q0 + r;
+        const uint32_t lane_base = (quarter * 32) << 16;
+        const uint32_t tQ = tmem + kTmemQ + lane_base;
+        const uint32_t tO = tmem + kTmemO + lane_base;
+        auto wait_all = [&](uint64_t* bar, uint32_t phase) {
+            return __all_sync(0xffffffffu, mbar_wait_lean(bar, phase, p.status)) != 0;
+        };
+        // Row r of unit u's Q (zeros past the sequence's queries).
+        auto load_q = [&](const Unit& u, float* v) {
             const PrefillSeq& sq = p.seq[u.s];
-            const bool row_live = qi < sq.q_tokens;
-            float v[kHD];
-            if (row_live) {
+            const uint64_t qi = u.q0 + r;
+            if (qi < sq.q_tokens) {
                 const float4* qrow = reinterpret_cast<const float4*>(sq.q + (qi * p.q_heads + u.qh) * kHD);
 #pragma unroll
                 for (int e = 0; e < kHD / 4; ++e) {
@@ -625,11 +629,10 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
 #pragma unroll
                 for (int e = 0; e < kHD; ++e) v[e] = 0.f;
             }
-            // The previous unit's last QK has read the Q columns. tcgen05.st
-            // is warp-collective: the wait result is made warp-uniform.
-            if (k >= 1 && !__all_sync(0xffffffffu, mbar_wait_lean(&q_free, (k - 1) & 1u, p.status))) break;
-            tc::fence_after_sync();
-            // Column c of the hi (lo) half holds dims 2c, 2c+1 of the row.
+        };
+        // Scaled hi/lo halves into the Q columns (column c of the hi (lo)
+        // half holds dims 2c, 2c+1), then publish.
+        auto write_q = [&](const float* v) {
 #pragma unroll
             for (uint32_t cc = 0; cc < kHD / 16; ++cc) {
                 uint32_t hi[8], lo[8];
@@ -642,6 +645,53 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
             tc::wait_st();
             tc::fence_before_sync();
             mbar_arrive(&q_full);
+        };
+        Unit cur, nxt;
+        uint32_t round = 0;
+        float v[kHD];
+        if (unit_at(p, round, cur)) {
+            load_q(cur, v);
+            write_q(v);  // the first unit's Q: the columns are free
+            for (uint32_t k = 0;; ++k) {
+                uint32_t nround = round + 1;
+                const bool more = unit_at(p, nround, nxt);
+                if (more) {
+                    // The next unit's Q, once this unit's last QK has read
+                    // the columns.
+                    load_q(nxt, v);
+                    if (!wait_all(&q_free, k & 1u)) break;
+                    tc::fence_after_sync();
+                    write_q(v);
+                }
+                // Epilogue of unit k: O from TMEM, released to the next
+                // unit's first PV as soon as it is in registers, then
+                // O / l to global memory.
+                if (!wait_all(&l_ready[k & 1u], (k >> 1) & 1u)) break;
+                if (!wait_all(&o_full, k & 1u)) break;
+                tc::fence_after_sync();
+#pragma unroll
+                for (int cb = 0; cb < kHD; cb += 32) tc::ld32(tO + cb, v + cb);
+                tc::wait_ld32(v);
+                tc::reg_fence32(v + 32);
+                tc::reg_fence32(v + 64);
+                tc::reg_fence32(v + 96);
+                tc::fence_before_sync();
+                mbar_arrive(&o_free);
+                const float inv = 1.f / l_sh[k & 1u][r];
+                mbar_arrive(&l_free[k & 1u]);
+                const PrefillSeq& sq = p.seq[cur.s];
+                const uint64_t qi = cur.q0 + r;
+                if (qi < sq.q_tokens) {
+                    float4* orow = reinterpret_cast<float4*>(sq.o + (qi * p.q_heads + cur.qh) * kHD);
+#pragma unroll
+                    for (int e = 0; e < kHD / 4; ++e)
+                        orow[e] = make_float4(v[4 * e] * inv, v[4 * e + 1] * inv, v[4 * e + 2] * inv,
+                                              v[4 * e + 3] * inv);
+                }
+                if (!more) break;
+                cur = nxt;
+                round = nround;
+            }
         }
     }
 
