@@ -47,6 +47,7 @@
 // Semantics: KVFlux src/v2/paged_attention.cu:109-128 (query i sees
 // positions <= kv_tokens - query_tokens + i; KV head = q_head / group).
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <type_traits>
 
@@ -721,16 +722,16 @@ cudaError_t launch_prefill_tc_batch(const CacheView& c, const AttentionArgs* seq
     cudaError_t err = cudaSuccess;
     const CacheMaps* maps = cache_maps(c, &err);
     if (maps == nullptr) return err != cudaSuccess ? err : cudaErrorInvalidValue;
-    static bool attr_done[64] = {false};
+    static std::atomic<int> attr_done[64];  // zero-initialised; callers on several threads set the same attribute
     const bool bf = c.dtype == KVFX_BF16;
-    if (c.device < 0 || c.device >= 64 || !attr_done[c.device]) {
+    if (c.device < 0 || c.device >= 64 || !attr_done[c.device].load(std::memory_order_acquire)) {
         err = cudaFuncSetAttribute(prefill_tc_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    kSmemAlloc);
         if (err != cudaSuccess) return err;
         err = cudaFuncSetAttribute(prefill_tc_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    kSmemAlloc);
         if (err != cudaSuccess) return err;
-        if (c.device >= 0 && c.device < 64) attr_done[c.device] = true;
+        if (c.device >= 0 && c.device < 64) attr_done[c.device].store(1, std::memory_order_release);
     }
     const int sms = device_sm_count(c.device);
     if (sms <= 0) return cudaErrorInvalidDevice;
