@@ -392,7 +392,11 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
             };
             constexpr uint32_t kSplit = 12;  // MMAs of a step issued before the next step's waits
             bool ok = true;
-            for (int i = 0; i < 2 && ok && qk.valid; ++i) {  // QK(0), QK(1)
+            // QK(0), QK(1). Loops here and below keep one copy of each MMA
+            // group in the code: the kernel's roles share the SM's
+            // instruction cache.
+#pragma unroll 1
+            for (int i = 0; i < 2 && ok && qk.valid; ++i) {
                 ok = qk_wait();
                 if (ok) {
                     qk_mmas(0, 16);
@@ -403,21 +407,17 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
             // Steady state: PV(g), then QK(g + 2).
             while (ok && pv.valid) {
                 const bool more_qk = qk.valid;
-                if (more_qk && qk.j == 0) {
-                    // QK(g + 2) starts a unit: its Q is staged by the warps
-                    // that also run the epilogue, after the epilogue of the
-                    // unit before the previous one, which may be waiting for
-                    // this PV's commit (when the previous unit has one tile).
-                    // So PV(g) is issued and committed before that wait.
-                    pv_mmas(0, 16);
-                    pv_finish();
-                    ok = qk_wait();
-                } else {
-                    pv_mmas(0, kSplit);
-                    if (more_qk) ok = qk_wait();
-                    pv_mmas(kSplit, 16);
-                    pv_finish();
-                }
+                // When QK(g + 2) starts a unit, its Q is staged by the warps
+                // that also run the epilogue, after the epilogue of the unit
+                // before the previous one, which may be waiting for this
+                // PV's commit (when the previous unit has one tile): then
+                // PV(g) is issued and committed before that wait.
+                const bool unit_start = more_qk && qk.j == 0;
+                pv_mmas(0, kSplit);
+                if (more_qk && !unit_start) ok = qk_wait();
+                pv_mmas(kSplit, 16);
+                pv_finish();
+                if (unit_start) ok = qk_wait();
                 if (!ok) break;
                 if (more_qk) {
                     // All of QK(g + 2) and its commit before the wait for
@@ -647,49 +647,58 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
             tc::fence_before_sync();
             mbar_arrive(&q_full);
         };
-        Unit cur, nxt;
-        uint32_t round = 0;
+        // Epilogue of unit k (u): O from TMEM, released to the next unit's
+        // first PV as soon as it is in registers, then O / l to global
+        // memory. Uses v as its buffer.
         float v[kHD];
-        if (unit_at(p, round, cur)) {
-            load_q(cur, v);
-            write_q(v);  // the first unit's Q: the columns are free
-            for (uint32_t k = 0;; ++k) {
-                uint32_t nround = round + 1;
-                const bool more = unit_at(p, nround, nxt);
-                if (more) {
-                    // The next unit's Q, once this unit's last QK has read
-                    // the columns.
-                    load_q(nxt, v);
-                    if (!wait_all(&q_free, k & 1u)) break;
-                    tc::fence_after_sync();
-                    write_q(v);
-                }
-                // Epilogue of unit k: O from TMEM, released to the next
-                // unit's first PV as soon as it is in registers, then
-                // O / l to global memory.
-                if (!wait_all(&l_ready[k & 1u], (k >> 1) & 1u)) break;
-                if (!wait_all(&o_full, k & 1u)) break;
+        auto epilogue = [&](uint32_t k, const Unit& u) -> bool {
+            if (!wait_all(&l_ready[k & 1u], (k >> 1) & 1u)) return false;
+            if (!wait_all(&o_full, k & 1u)) return false;
+            tc::fence_after_sync();
+#pragma unroll
+            for (int cb = 0; cb < kHD; cb += 32) tc::ld32(tO + cb, v + cb);
+            tc::wait_ld32(v);
+            tc::reg_fence32(v + 32);
+            tc::reg_fence32(v + 64);
+            tc::reg_fence32(v + 96);
+            tc::fence_before_sync();
+            mbar_arrive(&o_free);
+            const float inv = 1.f / l_sh[k & 1u][r];
+            mbar_arrive(&l_free[k & 1u]);
+            const PrefillSeq& sq = p.seq[u.s];
+            const uint64_t qi = u.q0 + r;
+            if (qi < sq.q_tokens) {
+                float4* orow = reinterpret_cast<float4*>(sq.o + (qi * p.q_heads + u.qh) * kHD);
+#pragma unroll
+                for (int e = 0; e < kHD / 4; ++e)
+                    orow[e] = make_float4(v[4 * e] * inv, v[4 * e + 1] * inv, v[4 * e + 2] * inv,
+                                          v[4 * e + 3] * inv);
+            }
+            return true;
+        };
+        // One pass per unit k: Q(k) into TMEM (the columns are free for the
+        // first unit, else once unit k - 1's last QK has read them), then
+        // the epilogue of unit k - 1, then the loads of Q(k + 1). One call
+        // site each keeps the code small (the roles share the SM's
+        // instruction cache).
+        Unit cur, nxt, prev;
+        uint32_t round = 0;
+        bool have = unit_at(p, round, cur);
+        if (have) load_q(cur, v);
+#pragma unroll 1
+        for (uint32_t k = 0;; ++k) {
+            if (have) {
+                if (k >= 1 && !wait_all(&q_free, (k - 1) & 1u)) break;
                 tc::fence_after_sync();
-#pragma unroll
-                for (int cb = 0; cb < kHD; cb += 32) tc::ld32(tO + cb, v + cb);
-                tc::wait_ld32(v);
-                tc::reg_fence32(v + 32);
-                tc::reg_fence32(v + 64);
-                tc::reg_fence32(v + 96);
-                tc::fence_before_sync();
-                mbar_arrive(&o_free);
-                const float inv = 1.f / l_sh[k & 1u][r];
-                mbar_arrive(&l_free[k & 1u]);
-                const PrefillSeq& sq = p.seq[cur.s];
-                const uint64_t qi = cur.q0 + r;
-                if (qi < sq.q_tokens) {
-                    float4* orow = reinterpret_cast<float4*>(sq.o + (qi * p.q_heads + cur.qh) * kHD);
-#pragma unroll
-                    for (int e = 0; e < kHD / 4; ++e)
-                        orow[e] = make_float4(v[4 * e] * inv, v[4 * e + 1] * inv, v[4 * e + 2] * inv,
-                                              v[4 * e + 3] * inv);
-                }
-                if (!more) break;
+                write_q(v);
+            }
+            if (k >= 1 && !epilogue(k - 1, prev)) break;
+            if (!have) break;
+            prev = cur;
+            uint32_t nround = round + 1;
+            have = unit_at(p, nround, nxt);
+            if (have) {
+                load_q(nxt, v);
                 cur = nxt;
                 round = nround;
             }
