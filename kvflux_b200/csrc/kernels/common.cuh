@@ -14,6 +14,23 @@
 
 namespace kvfx {
 
+// --------------------------------------------------------------- division ---
+
+// n / d for n < 2^31 with one multiply-high: m = floor(2^32 (2^s - d) / d) + 1,
+// s = ceil(log2 d) (the round-up multiplier of Granlund and Montgomery, 1994).
+struct FastDiv {
+    uint32_t m, s;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+    uint32_t s = 0;
+    while ((1ull << s) < d) ++s;
+    const uint64_t m = ((1ull << 32) * ((1ull << s) - d)) / d + 1;
+    return FastDiv{static_cast<uint32_t>(m), s};
+}
+
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, FastDiv f) { return (__umulhi(n, f.m) + n) >> f.s; }
+
 // ---------------------------------------------------------------- status ---
 
 // Set bits of the per-device status word (mapped host memory, or a
@@ -261,6 +278,11 @@ __device__ __forceinline__ void f2_unpack(uint64_t x, float& a, float& b) {
 __device__ __forceinline__ uint64_t f2_add(uint64_t x, uint64_t y) {
     uint64_t r;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t x, uint64_t y) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
     return r;
 }
 __device__ __forceinline__ uint64_t f2_sub(uint64_t x, uint64_t y) {

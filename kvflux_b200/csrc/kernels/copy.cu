@@ -202,21 +202,6 @@ cudaError_t gather_simt_vb(const CacheView& c, const GatherArgs& a, unsigned* st
 constexpr int kGatherDirectThreads = 256;
 constexpr int kGatherDirectPer = 8;
 
-// n / d for n < 2^31 with one multiply-high: m = floor(2^32 (2^s - d) / d) + 1,
-// s = ceil(log2 d) (the round-up multiplier of Granlund and Montgomery, 1994).
-struct FastDiv {
-    uint32_t m, s;
-};
-
-FastDiv make_fastdiv(uint32_t d) {
-    uint32_t s = 0;
-    while ((1ull << s) < d) ++s;
-    const uint64_t m = ((1ull << 32) * ((1ull << s) - d)) / d + 1;
-    return FastDiv{static_cast<uint32_t>(m), s};
-}
-
-__device__ __forceinline__ uint32_t fast_div(uint32_t n, FastDiv f) { return (__umulhi(n, f.m) + n) >> f.s; }
-
 // One page of one sequence: n output vectors (tokens of the page x heads x
 // row vectors) from the page's K/V blocks ks/vs to the runs kd/vd; the same
 // loop as gather_direct_kernel's (kept written out there: as a call it costs

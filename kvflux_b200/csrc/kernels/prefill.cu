@@ -93,8 +93,10 @@ struct PrefillSeq {
 
 struct PrefillParams {
     PrefillSeq seq[kMaxPrefillSeqs];
-    uint64_t num_blocks, n_units;  // n_units: max query tiles x sequences x Q heads (shorter sequences leave gaps)
+    uint64_t num_blocks;
+    uint32_t n_units;  // max query tiles x sequences x Q heads (shorter sequences leave gaps), < 2^31
     uint32_t num_seqs, q_heads, kv_heads, group;
+    FastDiv div_round, div_qheads, div_group;  // by num_seqs x q_heads, q_heads, group
     float qscale;
     unsigned* status;
 };
@@ -110,22 +112,24 @@ struct Unit {
 // sequences; an index past a shorter sequence's first tile is a gap, and the
 // CTA moves on to its next round (every role calls this with its own round
 // counter and skips the same gaps).
+// Inlined in every role, so kept small: unit indices stay below 2^31 (the
+// host checks) and the three divisions are multiply-highs by constants the
+// host prepares.
 __device__ __forceinline__ bool unit_at(const PrefillParams& p, uint32_t& round, Unit& u) {
-    const uint64_t G = gridDim.x;
+    const uint32_t G = gridDim.x;
     for (;; ++round) {
         const uint64_t base = static_cast<uint64_t>(round) * G;
         if (base >= p.n_units) return false;
-        const uint64_t idx = base + ((round & 1u) ? (G - 1 - blockIdx.x) : blockIdx.x);
+        const uint32_t idx = static_cast<uint32_t>(base) + ((round & 1u) ? (G - 1 - blockIdx.x) : blockIdx.x);
         if (idx >= p.n_units) return false;  // partial last round
-        const uint64_t per_round = static_cast<uint64_t>(p.num_seqs) * p.q_heads;
-        const uint64_t ur = idx / per_round;
-        const uint32_t rem = static_cast<uint32_t>(idx - ur * per_round);
-        u.s = rem / p.q_heads;
+        const uint32_t ur = fast_div(idx, p.div_round);
+        const uint32_t rem = idx - ur * (p.num_seqs * p.q_heads);
+        u.s = fast_div(rem, p.div_qheads);
         u.qh = rem - u.s * p.q_heads;
         const PrefillSeq& sq = p.seq[u.s];
         const uint64_t nq = ceil_div(sq.q_tokens, kBM);
         if (ur >= nq) continue;
-        u.kh = u.qh / p.group;
+        u.kh = fast_div(u.qh, p.div_group);
         u.q0 = (nq - 1 - ur) * kBM;
         const uint64_t q_last = umin64(u.q0 + kBM, sq.q_tokens) - 1;
         u.ntiles = static_cast<uint32_t>((sq.kv_tokens - sq.q_tokens + q_last) / kBN + 1);
@@ -613,33 +617,40 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
             return __all_sync(0xffffffffu, mbar_wait_lean(bar, phase, p.status)) != 0;
         };
         // Row r of unit u's Q (zeros past the sequence's queries).
+        // Rows past the sequence's queries load its last query row instead:
+        // their scores, weights and O rows stay in their own TMEM lanes and
+        // are never stored (and no branch duplicates the load code).
         auto load_q = [&](const Unit& u, float* v) {
             const PrefillSeq& sq = p.seq[u.s];
-            const uint64_t qi = u.q0 + r;
-            if (qi < sq.q_tokens) {
-                const float4* qrow = reinterpret_cast<const float4*>(sq.q + (qi * p.q_heads + u.qh) * kHD);
+            const uint64_t qi = umin64(u.q0 + r, sq.q_tokens - 1);
+            const float4* qrow = reinterpret_cast<const float4*>(sq.q + (qi * p.q_heads + u.qh) * kHD);
 #pragma unroll
-                for (int e = 0; e < kHD / 4; ++e) {
-                    const float4 x = __ldg(qrow + e);
-                    v[4 * e] = x.x;
-                    v[4 * e + 1] = x.y;
-                    v[4 * e + 2] = x.z;
-                    v[4 * e + 3] = x.w;
-                }
-            } else {
-#pragma unroll
-                for (int e = 0; e < kHD; ++e) v[e] = 0.f;
+            for (int e = 0; e < kHD / 4; ++e) {
+                const float4 x = __ldg(qrow + e);
+                v[4 * e] = x.x;
+                v[4 * e + 1] = x.y;
+                v[4 * e + 2] = x.z;
+                v[4 * e + 3] = x.w;
             }
         };
         // Scaled hi/lo halves into the Q columns (column c of the hi (lo)
         // half holds dims 2c, 2c+1), then publish.
+        const uint64_t qs2 = f2_pack(p.qscale, p.qscale);
         auto write_q = [&](const float* v) {
 #pragma unroll
             for (uint32_t cc = 0; cc < kHD / 16; ++cc) {
                 uint32_t hi[8], lo[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    split2_fast<T>(v[16 * cc + 2 * e] * p.qscale, v[16 * cc + 2 * e + 1] * p.qscale, hi[e], lo[e]);
+                for (int e = 0; e < 8; ++e) {
+                    // Packed f32x2 arithmetic: the same split as split2_fast.
+                    const uint64_t x = f2_mul(f2_pack(v[16 * cc + 2 * e], v[16 * cc + 2 * e + 1]), qs2);
+                    float x0, x1;
+                    f2_unpack(x, x0, x1);
+                    hi[e] = Elem<T>::pack(x0, x1);
+                    float r0, r1;
+                    f2_unpack(f2_sub(x, widen2<T>(hi[e])), r0, r1);
+                    lo[e] = Elem<T>::pack(r0, r1);
+                }
                 tc::st8(tQ + cc * 8, hi);
                 tc::st8(tQ + kHD / 2 + cc * 8, lo);
             }
@@ -717,7 +728,7 @@ bool prefill_eligible(const CacheView& c, const AttentionArgs& a) {
     return (c.dtype == KVFX_BF16 || c.dtype == KVFX_F16) && c.bs == 16 && c.hd == kHD && a.query_tokens >= 2 &&
            a.q_heads % c.heads == 0 && c.num_blocks < (1ull << 31) &&
            reinterpret_cast<uintptr_t>(a.q) % 16 == 0 && reinterpret_cast<uintptr_t>(a.o) % 16 == 0 &&
-           ceil_div(a.query_tokens, kBM) < (1ull << 31);
+           ceil_div(a.query_tokens, kBM) * a.q_heads < (1ull << 26);  // a launch's units stay below 2^31
 }
 
 }  // namespace
@@ -755,7 +766,12 @@ cudaError_t launch_prefill_tc_batch(const CacheView& c, const AttentionArgs* seq
     p.q_heads = seqs[0].q_heads;
     p.kv_heads = c.heads;
     p.group = p.q_heads / c.heads;
-    p.n_units = max_qtiles * n * p.q_heads;
+    const uint64_t n_units = max_qtiles * n * p.q_heads;
+    if (n_units >= (1ull << 31)) return cudaErrorInvalidValue;  // each sequence is checked below 2^26
+    p.n_units = static_cast<uint32_t>(n_units);
+    p.div_round = make_fastdiv(n * p.q_heads);
+    p.div_qheads = make_fastdiv(p.q_heads);
+    p.div_group = make_fastdiv(p.group);
     p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.hd)));
     p.status = status;
     const unsigned grid = static_cast<unsigned>(umin64(p.n_units, static_cast<uint64_t>(sms)));
