@@ -173,15 +173,31 @@ decode_mma_kernel(const __grid_constant__ DecodeParams p, const __grid_constant_
     }
     __syncwarp();
 
-    auto issue = [&](uint32_t i) {  // lane 0: load page i of this warp
+    // This warp's page ids, read once up front: lane l holds those of its
+    // pages l and l + 32 (splits of up to 64 pages per warp; longer ones read
+    // each id when its page is issued), so a ring slot's refill does not wait
+    // for a table read.
+    const bool ids_cached = n_my <= 64;
+    uint64_t id_lo = 0, id_hi = 0;
+    if (ids_cached) {
+        const uint64_t j0 = pbeg + warp + static_cast<uint64_t>(kWarps) * lane;
+        const uint64_t j1 = j0 + static_cast<uint64_t>(kWarps) * 32;
+        if (lane < n_my) id_lo = append ? __ldcg(row + j0) : __ldg(row + j0);
+        if (lane + 32 < n_my) id_hi = append ? __ldcg(row + j1) : __ldg(row + j1);
+    }
+    auto issue = [&](uint32_t i) {  // whole warp; lane 0 issues the copies of page i of this warp
         if (i >= n_my) return;
         const uint64_t j = pbeg + warp + static_cast<uint64_t>(kWarps) * i;
         uint64_t blk;
-        if (!append) {
-            blk = __ldg(row + j);
+        if (ids_cached) {
+            blk = __shfl_sync(0xffffffffu, i < 32 ? id_lo : id_hi, i & 31);
+        } else if (lane == 0) {
+            blk = append ? __ldcg(row + j) : __ldg(row + j);
         } else {
-            blk = j == last && new_blk != ~0ull ? new_blk : __ldcg(row + j);
+            blk = 0;
         }
+        if (append && j == last && new_blk != ~0ull) blk = new_blk;
+        if (lane != 0) return;
         if (blk >= p.num_blocks) {
             raise_flag(p.status, KVFX_FLAG_BAD_INDEX);
             blk = 0;
@@ -197,10 +213,8 @@ decode_mma_kernel(const __grid_constant__ DecodeParams p, const __grid_constant_
                         static_cast<int>(blk), &bars[warp][st]);
         }
     };
-    if (lane == 0) {
 #pragma unroll
-        for (int i = 0; i < kStages; ++i) issue(i);
-    }
+    for (int i = 0; i < kStages; ++i) issue(i);
 
     // Q fragments (A operand): rows g = hi(Q[g]), rows g+8 = lo(Q[g]).
     const int g = lane >> 2, tig = lane & 3;
@@ -324,7 +338,7 @@ decode_mma_kernel(const __grid_constant__ DecodeParams p, const __grid_constant_
             }
         }
         __syncwarp();
-        if (lane == 0) issue(i + kStages);
+        issue(i + kStages);
     }
 
     // ---- combine the 4 warps of this CTA (stage memory is free again) ----
