@@ -229,11 +229,10 @@ std::vector<TokenLocation> BatchDecodeSession::step_host(const void* key_host, c
     unsigned char* k_dev = io;
     unsigned char* v_dev = io + kv_al;
     auto* q_dev = reinterpret_cast<float*>(io + 2 * kv_al);
-    // Rows go in two chunks: the first eighth's inputs go up and its launch
+    // Rows go in two chunks: the first quarter's inputs go up and its launch
     // starts as soon as the pages are booked; the rest goes up on a side
-    // stream meanwhile and runs there concurrently (as paged_attention_batch_host;
-    // an eighth measured ~0.6 % faster per config-5 step than a quarter).
-    const std::size_t head_rows = batch >= 16 ? (batch + 7) / 8 : batch;
+    // stream meanwhile and runs there concurrently (as paged_attention_batch_host).
+    const std::size_t head_rows = batch >= 16 ? (batch + 3) / 4 : batch;
     auto upload = [&](std::size_t r0, std::size_t r1, cudaStream_t st) {
         if (r1 <= r0) return;
         detail::cuda_check(cudaMemcpyAsync(k_dev + r0 * kv_row, static_cast<const unsigned char*>(key_host) + r0 * kv_row,
