@@ -301,13 +301,11 @@ void batch_decode(const PagedKVStorage& storage, const std::vector<const Sequenc
     };
 
     // Device Q: one launch over every row. Host Q: two chunks, so that the
-    // kernel over the first eighth of the rows starts once its Q is up
+    // kernel over the first quarter of the rows starts once its Q is up
     // while the rest of Q goes up on a side stream, whose launch over the
     // other rows (own workspace, same split size) then runs concurrently
-    // and fills the SMs the first kernel's last CTAs leave idle. (An eighth
-    // exposes less upload time than a quarter; config 5, ms per call:
-    // 2.664-2.675 against 2.685-2.712.)
-    const std::size_t head_rows = host_io && batch >= 16 ? (batch + 7) / 8 : batch;
+    // and fills the SMs the first kernel's last CTAs leave idle.
+    const std::size_t head_rows = host_io && batch >= 16 ? (batch + 3) / 4 : batch;
     const std::size_t ws0 = workspace_of(0, head_rows);
     const std::size_t ws1 = head_rows < batch ? workspace_of(head_rows, batch) : 0;
     void* ws_head = rt.ensure_workspace(ws0, 0);
