@@ -533,26 +533,25 @@ prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant
                 uint64_t lsum0 = f2_pack(0.f, 0.f), lsum1 = lsum0;
                 auto p_chunk = [&](int c, float* v) {
                     if (masked) mask32(v, lim - 32 * c);
+                    // All 16 pairs of the chunk, then its hi and lo halves in
+                    // one 16-column store each.
+                    uint32_t hi[16], lo[16];
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        uint32_t hi[8], lo[8];
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) {
-                            float x0, x1;
-                            f2_unpack(f2_sub(f2_pack(v[16 * h + 2 * e], v[16 * h + 2 * e + 1]), mm), x0, x1);
-                            x0 = ex2_approx(x0);
-                            x1 = ex2_approx(x1);
-                            const uint64_t pe = f2_pack(x0, x1);
-                            if (e & 1) lsum1 = f2_add(lsum1, pe);
-                            else lsum0 = f2_add(lsum0, pe);
-                            hi[e] = Elem<T>::pack(x0, x1);
-                            float r0, r1;
-                            f2_unpack(f2_sub(pe, widen2<T>(hi[e])), r0, r1);
-                            lo[e] = Elem<T>::pack(r0, r1);
-                        }
-                        tc::st8(tS + 32 * c + 8 * h, hi);
-                        tc::st8(tS + 32 * c + 16 + 8 * h, lo);
+                    for (int e = 0; e < 16; ++e) {
+                        float x0, x1;
+                        f2_unpack(f2_sub(f2_pack(v[2 * e], v[2 * e + 1]), mm), x0, x1);
+                        x0 = ex2_approx(x0);
+                        x1 = ex2_approx(x1);
+                        const uint64_t pe = f2_pack(x0, x1);
+                        if (e & 1) lsum1 = f2_add(lsum1, pe);
+                        else lsum0 = f2_add(lsum0, pe);
+                        hi[e] = Elem<T>::pack(x0, x1);
+                        float r0, r1;
+                        f2_unpack(f2_sub(pe, widen2<T>(hi[e])), r0, r1);
+                        lo[e] = Elem<T>::pack(r0, r1);
                     }
+                    tc::st16(tS + 32 * c, hi);
+                    tc::st16(tS + 32 * c + 16, lo);
                 };
                 {
                     float va[32], vb[32];
